@@ -1,0 +1,416 @@
+#!/usr/bin/env python3
+"""Benchmark: Llama-3-8B-shaped prefill linears at TP = --gpus.
+
+One step = the four linears of one decoder layer at M = 8192 tokens, BF16:
+qkv [6144 x 4096] and gate_up [28672 x 4096] column-parallel (N split over
+ranks, no communication), o_proj [4096 x 4096] and down [4096 x 14336]
+row-parallel (K split, NCCL all-reduce of BF16 partials, chunked so the
+all-reduce overlaps the next GEMM chunk). 3573 GFLOP per step for the whole
+job, whatever the rank count (strong scaling).
+
+    python bench.py                          # N=1, defaults
+    torchrun --nproc-per-node N bench.py --gpus N --steps K --warmup W
+    python bench.py --impl reference         # the reference's CPU path (host cores)
+
+Prints one JSON line on rank 0. `value` = whole-job TFLOP/s, device-timed
+with CUDA events between barriers, max over ranks; `e2e` = the same step
+through the C ABI with the input activations copied from pinned host memory
+and the layer output copied back inside the timed region (copies on their
+own streams, double-buffered). Inputs are larger than L2 (126 MB) every
+step, so no explicit flush is done.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Prefill GEMM TFLOP/s/GPU (% of BF16 dense peak) at TP 1/2/4/8; decode GB/s"
+TOKENS = 8192
+MEASURED_PEAKS = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM traffic per launch of the dominant kernel (gate_up, 128x256 persistent
+# tcgen05 kernel) from one ncu capture; see profiles/ for the capture and the
+# scaling from the captured case. None until a capture exists.
+GATE_UP_TRAFFIC_BYTES = None
+
+NVML_REASONS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+    0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+    0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+}
+
+
+def load_peaks() -> tuple[dict, str]:
+    try:
+        return json.loads(MEASURED_PEAKS.read_text()), "measured"
+    except Exception:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while running."""
+
+    def __init__(self, device_index: int, period_s: float = 0.05) -> None:
+        self.idx, self.period = device_index, period_s
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._nv = pynvml
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        except Exception:
+            self._nv = None
+        return self
+
+    def _run(self) -> None:
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+        return False
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        mhz = [s[0] for s in self.samples]
+        bits = 0
+        for _, r in self.samples:
+            bits |= r
+        reasons = sorted(name for b, name in NVML_REASONS.items() if bits & b and name != "gpu_idle")
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(mhz)}
+
+
+# ---------------------------------------------------------------- CPU path
+
+
+def cpu_layer_sample(rows: int, dtype_name: str = "bf16"):
+    """The four linears of the layer on `rows` tokens on the host cores, through
+    the reference's CPU path (overlay fallback = F.linear), restated in oracle/."""
+    import torch
+
+    from oracle import overlay_fallback
+    from zcutlass_b200.tp import LLAMA3_8B as S
+
+    dt = torch.bfloat16 if dtype_name == "bf16" else torch.float16
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(rows, S.hidden, generator=g).to(dt)
+    w = {
+        "qkv": (torch.randn(S.qkv_out, S.hidden, generator=g) * S.hidden ** -0.5).to(dt),
+        "gate_up": (torch.randn(2 * S.intermediate, S.hidden, generator=g) * S.hidden ** -0.5).to(dt),
+        "o": (torch.randn(S.hidden, S.o_in, generator=g) * S.o_in ** -0.5).to(dt),
+        "down": (torch.randn(S.hidden, S.intermediate, generator=g) * S.intermediate ** -0.5).to(dt),
+    }
+
+    def step():
+        qkv = overlay_fallback.linear(x, w["qkv"])
+        gu = overlay_fallback.linear(x, w["gate_up"])
+        overlay_fallback.linear(qkv[:, : S.o_in], w["o"])
+        return overlay_fallback.linear(gu[:, : S.intermediate], w["down"])
+
+    return step, S.flops(rows)
+
+
+def cpu_throughput(budget_s: float, steps: int | None = None, warmup: int = 1) -> dict:
+    """Times the CPU path on a bounded sample: TFLOP/s with all host threads."""
+    import torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    step, flops = cpu_layer_sample(64)
+    t0 = time.perf_counter()
+    step()
+    per_row_s = (time.perf_counter() - t0) / 64
+    n_steps = steps if steps is not None else 10
+    rows = int(max(16, min(TOKENS, budget_s / max(n_steps + warmup, 1) / max(per_row_s, 1e-9))))
+    step, flops = cpu_layer_sample(rows)
+    for _ in range(warmup):
+        step()
+    times = []
+    for _ in range(n_steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    return {"value": flops / sec / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"layer linears on {rows} of {TOKENS} tokens (bf16 F.linear on CPU, "
+                      f"{n_steps} timed steps, median {sec * 1e3:.1f} ms)",
+            "steps": n_steps, "ms_per_step": sec * 1e3}
+
+
+def run_reference(args) -> int:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    cb = cpu_throughput(budget_s=120.0, steps=args.steps, warmup=args.warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(cb["value"], 4), "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_step"],
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) activations, N(0,1/K) weights)",
+        "config": {"workload": "llama3-8b-layer-prefill-linears", "tokens": TOKENS, "model": "llama3-8b-shaped",
+                   "global_batch": TOKENS, "seq_len": TOKENS, "parallelism": "cpu"},
+        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": round(cb["value"], 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- GPU path
+
+
+def decode_sweep(device, peaks: dict, iters: int = 200) -> list[dict]:
+    """Llama-3-70B TP=8 per-GPU decode linears on one GPU:
+    achieved HBM GB/s, weights rotated over > 2x L2 so every launch streams HBM."""
+    import torch
+
+    from zcutlass_b200 import _native
+
+    shapes = {"qkv": (1280, 8192), "o_proj": (8192, 1024), "gate_up": (7168, 8192), "down": (8192, 3584)}
+    out = []
+    stream = torch.cuda.current_stream(device).cuda_stream
+    for name, (n, k) in shapes.items():
+        wbytes = n * k * 2
+        copies = max(2, -(-3 * 126 * 2**20 // wbytes))
+        ws = [torch.randn(n, k, device=device, dtype=torch.bfloat16) * k ** -0.5 for _ in range(copies)]
+        for m in (1, 8, 16, 32):
+            x = torch.randn(m, k, device=device, dtype=torch.bfloat16)
+            d = torch.empty(m, n, device=device, dtype=torch.bfloat16)
+            descs = [_native.make_desc(m, n, k, k, k, n, n, _native.BF16, stream=stream,
+                                       b_layout=_native.COLUMN_MAJOR) for _ in ws]
+
+            def run(i):
+                st = _native.gemm(descs[i % copies], x.data_ptr(), ws[i % copies].data_ptr(), None, d.data_ptr())
+                assert st == 0, st
+
+            for i in range(2 * copies):
+                run(i)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(iters):
+                run(i)
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / iters
+            nbytes = 2 * (m * k + n * k + m * n)
+            gbs = nbytes / (us * 1e-6) / 1e9
+            sel = _native.selected_kernel(descs[0])["kernel_name"]
+            out.append({"linear": name, "m": m, "n": n, "k": k, "us": round(us, 2), "GB/s": round(gbs, 1),
+                        "frac_hbm": round(gbs / peaks["hbm_gbs"], 3), "kernel": sel})
+        del ws
+    return out
+
+
+def run_gpu(args) -> int:
+    import torch
+    import torch.distributed as dist
+
+    from zcutlass_b200 import _native, torch_ops
+    from zcutlass_b200.tp import LLAMA3_8B, TPDecoderLinears, TPGroup
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
+    torch_ops.load()
+    peaks, peaks_src = load_peaks()
+    tp = TPGroup.from_env()
+    layer = TPDecoderLinears(LLAMA3_8B, tp, device, torch.bfloat16, seed=0, chunks=args.chunks)
+    g = torch.Generator(device="cpu").manual_seed(1)
+    x_host = torch.randn(TOKENS, LLAMA3_8B.hidden, generator=g).to(torch.bfloat16)
+    x = x_host.to(device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        layer.forward(x)
+    barrier()
+
+    # ---- device-timed steps (inputs resident in HBM)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = _native.kernel_launches()
+    with ClockSampler(local) as clocks:
+        barrier()
+        start.record()
+        for i in range(args.steps):
+            layer.forward(x, events={"gate_up": ev[i]})
+        end.record()
+        torch.cuda.synchronize()
+    launches = _native.kernel_launches() - launches0
+    ms = max_over_ranks(start.elapsed_time(end)) / args.steps
+    barrier()
+    total_flops = LLAMA3_8B.flops(TOKENS)
+    value = total_flops / (ms * 1e-3) / 1e12
+    gate_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    gate_flops = 2.0 * TOKENS * layer.gate_up.weight.shape[0] * layer.gate_up.weight.shape[1]
+    gate_tflops = gate_flops / (gate_ms * 1e-3) / 1e12
+    peak = peaks["bf16_tflops_sustained"]
+
+    # ---- end to end through the C ABI with pinned host buffers
+    e2e = run_e2e(args, layer, x_host, device, barrier, max_over_ranks, total_flops)
+
+    line = None
+    if rank == 0:
+        cfg = {"workload": "llama3-8b-layer-prefill-linears", "model": "llama3-8b-shaped", "tokens": TOKENS,
+               "global_batch": TOKENS, "seq_len": TOKENS, "parallelism": f"tp{world}",
+               "linears": {"qkv": [6144, 4096], "o_proj": [4096, 4096], "gate_up": [28672, 4096],
+                           "down": [4096, 14336]},
+               "l2": "inputs larger than L2 every step (436 MB of weights per layer at TP1), no flush",
+               "allreduce_chunks": args.chunks}
+        sm = clocks.summary()
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) activations, N(0,1/K) weights)",
+            "config": cfg,
+            "per_gpu_tflops": round(value / world, 2),
+            "frac_of_bf16_peak_per_gpu": round(value / world / peak, 4),
+            "roofline": {"bound": "tensor", "kernel": "gate_up (zcutlass_sm100_tcgen05_bf16_128x256x64_ws_persistent)",
+                         "achieved": round(gate_tflops, 2), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(gate_tflops / peak, 4),
+                         "peak_source": f"bf16_tflops_sustained of {peaks_src} (burst {peaks['bf16_tflops']})",
+                         "frac_of_burst": round(gate_tflops / peaks["bf16_tflops"], 4),
+                         "algorithmic_flops_per_launch": gate_flops, "avg_launch_ms": round(gate_ms, 4),
+                         "traffic": GATE_UP_TRAFFIC_BYTES},
+            "clocks": sm,
+            "e2e": e2e,
+            "gpu_launches": launches,
+        }
+    if rank == 0 and world == 1 and not args.skip_decode:
+        line["decode"] = decode_sweep(device, peaks)
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        line["cpu_baseline"] = {k: v for k, v in cpu_throughput(budget_s=10.0).items()
+                                if k in ("value", "unit", "cores", "kind", "sample")}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_e2e(args, layer, x_host, device, barrier, max_over_ranks, total_flops) -> dict:
+    """Same step with host buffers: H2D of the layer input (pinned) on one copy
+    stream, D2H of the layer output on another, both double-buffered so the
+    copies of step i+1 / i-1 overlap the GEMMs of step i. All inside the timed region."""
+    import torch
+
+    compute = torch.cuda.current_stream(device)
+    h2d_s, d2h_s = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    hx = x_host.pin_memory()
+    dx = [torch.empty_like(hx, device=device) for _ in range(2)]
+    hidden = layer.shape.hidden
+    dout = [torch.empty(hx.shape[0], hidden, device=device, dtype=hx.dtype) for _ in range(2)]
+    hout = [torch.empty(hx.shape[0], hidden, dtype=hx.dtype).pin_memory() for _ in range(2)]
+    e = lambda: torch.cuda.Event()  # noqa: E731
+    h2d_ev, d2h_ev, comp_ev = [e(), e()], [e(), e()], [e(), e()]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = args.steps
+
+    def loop(n):
+        start.record(compute)
+        h2d_s.wait_event(start)
+        with torch.cuda.stream(h2d_s):
+            dx[0].copy_(hx, non_blocking=True)
+        h2d_ev[0].record(h2d_s)
+        for i in range(n):
+            s = i % 2
+            compute.wait_event(h2d_ev[s])
+            if i >= 2:
+                compute.wait_event(d2h_ev[s])
+            layer.forward(dx[s], out=dout[s])
+            comp_ev[s].record(compute)
+            if i + 1 < n:
+                if i >= 1:
+                    h2d_s.wait_event(comp_ev[1 - s])
+                with torch.cuda.stream(h2d_s):
+                    dx[1 - s].copy_(hx, non_blocking=True)
+                h2d_ev[1 - s].record(h2d_s)
+            d2h_s.wait_event(comp_ev[s])
+            with torch.cuda.stream(d2h_s):
+                hout[s].copy_(dout[s], non_blocking=True)
+            d2h_ev[s].record(d2h_s)
+        compute.wait_event(d2h_ev[(n - 1) % 2])
+        end.record(compute)
+        torch.cuda.synchronize()
+
+    loop(min(3, steps))
+    barrier()
+    loop(steps)
+    ms = max_over_ranks(start.elapsed_time(end)) / steps
+    barrier()
+    nbytes = hx.numel() * hx.element_size()
+    return {"value": round(total_flops / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
+            "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": dout[0].numel() * dout[0].element_size(),
+            "api": "C ABI zcutlass_gemm (include/zcutlass_c.h) via zcutlass_b200.tp"}
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["zcutlass", "reference"], default="zcutlass")
+    ap.add_argument("--chunks", type=int, default=4, help="row chunks of the row-parallel all-reduce")
+    ap.add_argument("--skip-decode", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_gpu(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

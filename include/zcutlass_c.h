@@ -1,0 +1,115 @@
+/*
+ * zcutlass C ABI: plain pointers, sizes and enums, no C++ or torch types.
+ *
+ * Every function below is a flat C entry point for the C++ API declared in
+ * include/zcutlass/gemm.hpp and is what an FFI (ctypes, cffi, JNI, cgo) binds.
+ * Each one cites the reference interface it replaces, in
+ * supercatking/zcutlass (paths relative to that project):
+ *
+ *   zcutlass_gemm               <- zcutlass::gemm(GemmDesc, A, B, C, D)
+ *                                  include/zcutlass/gemm/gemm.hpp:72-76, src/gemm.cu:609-629
+ *   zcutlass_gemm_rowmajor      <- same call with the GemmDesc fields passed flat
+ *                                  (what python/zcutlass_torch/csrc/zcutlass_torch.cpp:67-83 builds)
+ *   zcutlass_can_implement      <- zcutlass::can_implement(GemmArguments)  gemm.hpp:78, gemm.cu:718-739
+ *   zcutlass_get_workspace_size <- zcutlass::get_workspace_size            gemm.hpp:79, gemm.cu:741-744
+ *   zcutlass_selected_kernel_*  <- zcutlass::selected_kernel_*             gemm.hpp:80-88, gemm.cu:631-688
+ *   zcutlass_registered_gemm_operation_count <- gemm.hpp:89, gemm.cu:690-693
+ *   zcutlass_status_to_string   <- zcutlass::status_to_string              status.hpp:14
+ *   zcutlass_dtype_name / _bits <- numeric_types.hpp:43-44
+ *   zcutlass_version_*          <- gemm.hpp (umbrella) :13-15
+ *
+ * Entry points with no reference counterpart (Blackwell additions):
+ *   zcutlass_device_error       read/clear the device-side error word that the
+ *                               tcgen05 kernels set when a bounded wait expires
+ *   zcutlass_gemm_kernel_launches  number of kernel launches this library made
+ *
+ * Integer enum values equal the C++ enum values (Status, DType, LayoutKind).
+ * Return values of type int that carry a status use zcutlass_status values.
+ */
+#ifndef ZCUTLASS_C_H_
+#define ZCUTLASS_C_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* zcutlass::Status */
+enum zcutlass_status {
+  ZCUTLASS_SUCCESS = 0,
+  ZCUTLASS_INVALID_ARGUMENT = 1,
+  ZCUTLASS_NOT_SUPPORTED = 2,
+  ZCUTLASS_RUNTIME_ERROR = 3
+};
+
+/* zcutlass::DType */
+enum zcutlass_dtype {
+  ZCUTLASS_F16 = 0,
+  ZCUTLASS_BF16 = 1,
+  ZCUTLASS_F32 = 2,
+  ZCUTLASS_TF32 = 3,
+  ZCUTLASS_E4M3 = 4,
+  ZCUTLASS_E5M2 = 5,
+  ZCUTLASS_E2M1 = 6
+};
+
+/* zcutlass::layout::LayoutKind */
+enum zcutlass_layout { ZCUTLASS_ROW_MAJOR = 0, ZCUTLASS_COLUMN_MAJOR = 1 };
+
+/* Field-for-field C image of zcutlass::GemmDesc (same order). `stream` is a
+ * cudaStream_t passed as an opaque pointer (NULL = legacy default stream). */
+typedef struct zcutlass_gemm_desc {
+  int64_t m, n, k;
+  int64_t lda, ldb, ldc, ldd;
+  int32_t a_type, b_type, c_type, d_type;
+  float alpha, beta;
+  const void* bias;
+  void* stream;
+  int32_t a_layout, b_layout, c_layout, d_layout;
+} zcutlass_gemm_desc;
+
+int zcutlass_gemm(const zcutlass_gemm_desc* desc, const void* A, const void* B, const void* C,
+                  void* D);
+
+/* Row-major GEMM with every argument flat; all four tensors share `dtype`. */
+int zcutlass_gemm_rowmajor(int64_t m, int64_t n, int64_t k, const void* A, int64_t lda,
+                           const void* B, int64_t ldb, const void* C, int64_t ldc, void* D,
+                           int64_t ldd, int32_t dtype, float alpha, float beta,
+                           const void* bias, void* stream);
+
+int zcutlass_can_implement(const zcutlass_gemm_desc* desc, const void* A, const void* B,
+                           const void* C, const void* D);
+size_t zcutlass_get_workspace_size(const zcutlass_gemm_desc* desc);
+
+const char* zcutlass_selected_kernel_name(const zcutlass_gemm_desc* desc);
+const char* zcutlass_selected_kernel_family(const zcutlass_gemm_desc* desc);
+const char* zcutlass_selected_kernel_path(const zcutlass_gemm_desc* desc);
+int zcutlass_selected_kernel_tile_m(const zcutlass_gemm_desc* desc);
+int zcutlass_selected_kernel_tile_n(const zcutlass_gemm_desc* desc);
+int zcutlass_selected_kernel_tile_k(const zcutlass_gemm_desc* desc);
+int zcutlass_selected_kernel_pipeline_stages(const zcutlass_gemm_desc* desc);
+const char* zcutlass_selected_kernel_epilogue_kind(const zcutlass_gemm_desc* desc);
+int zcutlass_registered_gemm_operation_count(void);
+
+const char* zcutlass_status_to_string(int status);
+const char* zcutlass_dtype_name(int dtype);
+int zcutlass_dtype_bits(int dtype);
+int zcutlass_version_major(void);
+int zcutlass_version_minor(void);
+int zcutlass_version_patch(void);
+
+/* Device-side error word of the current device: 0 when clean, otherwise a code
+ * (site * 16 + role) written by the first kernel whose bounded wait expired.
+ * Synchronises the device. `clear` != 0 resets the word to 0 afterwards. */
+int zcutlass_device_error(int clear);
+
+/* Number of kernel launches this library has enqueued since load (all devices). */
+uint64_t zcutlass_gemm_kernel_launches(void);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* ZCUTLASS_C_H_ */

@@ -1,0 +1,132 @@
+"""In-tree build of the native libraries (no JIT cache, no pip install).
+
+    python -m zcutlass_b200.build            # core library + torch operators
+    python -m zcutlass_b200.build --oracle   # also the test oracle (oracle/Makefile)
+
+Outputs (git-ignored, shipped alongside the sources):
+    zcutlass_b200/libzcutlass.so        kernels, dispatcher, C ABI (include/zcutlass_c.h)
+    zcutlass_b200/libzcutlass_torch.so  torch.ops.zcutlass_torch.* / torch.ops.zcutlass.*
+
+Every CUDA source is compiled for sm_100a only
+(-gencode arch=compute_100a,code=sm_100a); host sources go through g++.
+Rebuilds are incremental on file modification times.
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+INCLUDE = ROOT / "include"
+BUILD = PKG / "_build"
+CORE_SO = PKG / "libzcutlass.so"
+TORCH_SO = PKG / "libzcutlass_torch.so"
+
+CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
+NVCC = str(CUDA_HOME / "bin" / "nvcc")
+CXX = os.environ.get("CXX", "g++")
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+CORE_HOST_SRCS = ["foundation.cpp", "gemm.cpp", "c_abi.cpp", "tma_desc.cpp"]
+CORE_CUDA_SRCS = ["launchers.cu"]
+
+
+def _headers() -> list[Path]:
+    return sorted(list(CSRC.rglob("*.hpp")) + list(CSRC.rglob("*.cuh")) + list(INCLUDE.rglob("*.h*")))
+
+
+def _stale(target: Path, deps: list[Path]) -> bool:
+    if not target.exists():
+        return True
+    t = target.stat().st_mtime
+    return any(d.stat().st_mtime > t for d in deps)
+
+
+def _run(cmd: list[str], verbose: bool) -> None:
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+
+
+def build_core(verbose: bool = False) -> Path:
+    BUILD.mkdir(exist_ok=True)
+    headers = _headers()
+    objs: list[Path] = []
+    incs = [f"-I{INCLUDE}", f"-I{CSRC}", f"-I{CUDA_HOME / 'include'}"]
+    for src in CORE_HOST_SRCS:
+        s = CSRC / src
+        o = BUILD / (s.stem + ".o")
+        if _stale(o, [s, *headers]):
+            _run([CXX, "-std=c++17", "-O2", "-fPIC", "-Wall", "-c", str(s), "-o", str(o), *incs], verbose)
+        objs.append(o)
+    for src in CORE_CUDA_SRCS:
+        s = CSRC / src
+        o = BUILD / (s.stem + ".cu.o")
+        if _stale(o, [s, *headers]):
+            _run([NVCC, "-std=c++17", "-O3", "-lineinfo", *ARCH_FLAGS, "-Xcompiler", "-fPIC",
+                  "-c", str(s), "-o", str(o), *incs], verbose)
+        objs.append(o)
+    if _stale(CORE_SO, objs):
+        _run([NVCC, "-shared", *ARCH_FLAGS, "-o", str(CORE_SO), *map(str, objs),
+              "-Xlinker", "-Bsymbolic", "-lcudart"], verbose)
+    return CORE_SO
+
+
+def build_torch_ops(verbose: bool = False) -> Path:
+    import torch
+    from torch.utils import cpp_extension
+
+    build_core(verbose)
+    src = CSRC / "torch_ext.cpp"
+    obj = BUILD / "torch_ext.o"
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    incs = [f"-I{p}" for p in cpp_extension.include_paths()] + [f"-I{INCLUDE}", f"-I{CUDA_HOME / 'include'}"]
+    if _stale(obj, [src, *_headers()]):
+        _run([CXX, "-std=c++17", "-O2", "-fPIC", f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_API_INCLUDE_EXTENSION_H",
+              "-c", str(src), "-o", str(obj), *incs], verbose)
+    if _stale(TORCH_SO, [obj, CORE_SO]):
+        libdirs = [f"-L{p}" for p in cpp_extension.library_paths()]
+        _run([CXX, "-shared", "-o", str(TORCH_SO), str(obj), *libdirs, f"-L{PKG}", "-lzcutlass",
+              "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda",
+              f"-L{CUDA_HOME / 'lib64'}", "-lcudart", "-Wl,-rpath,$ORIGIN"], verbose)
+    return TORCH_SO
+
+
+def build_oracle(verbose: bool = False) -> None:
+    """Builds oracle/liboracle.so and, when the reference sources exist,
+    oracle/_ref/libzcutlass_ref.so (test infrastructure only)."""
+    oracle = ROOT / "oracle"
+    make = shutil.which("make")
+    if make is None:
+        raise RuntimeError("make is required to build the oracle")
+    _run([make, "-s", "-C", str(oracle)], verbose)
+    ref_root = Path(os.environ.get("ZCUTLASS_REF_ROOT", "/root/reference"))
+    if (ref_root / "src" / "gemm.cu").exists():
+        _run([make, "-s", "-C", str(oracle), "ref", f"REF_ROOT={ref_root}"], verbose)
+
+
+def build_all(oracle: bool = True, verbose: bool = False) -> None:
+    build_core(verbose)
+    build_torch_ops(verbose)
+    if oracle:
+        build_oracle(verbose)
+
+
+def main(argv: list[str] | None = None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--oracle", action="store_true", help="also build the test oracle")
+    ap.add_argument("-v", "--verbose", action="store_true")
+    args = ap.parse_args(argv)
+    build_all(oracle=args.oracle, verbose=args.verbose)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

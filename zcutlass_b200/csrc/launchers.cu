@@ -1,0 +1,267 @@
+// Kernel instantiation and launch. Compiled for sm_100a only.
+#include "launchers.hpp"
+
+#include <algorithm>
+#include <atomic>
+#include <mutex>
+
+#include "kernels/generic_gemm.cuh"
+#include "kernels/sm100_umma_gemm.cuh"
+#include "kernels/sm100_umma_swapab.cuh"
+#include "tma_desc.hpp"
+
+namespace zcb {
+
+// One error word per device (each device loading the library gets its own
+// copy of this variable). Kernels set it when a bounded wait expires.
+__device__ int g_device_error_word = 0;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::atomic<uint64_t> g_launches{0};
+
+struct DeviceSlot {
+  std::once_flag once;
+  DeviceInfo info;
+  // Bit i set once cudaFuncSetAttribute ran for kernel configuration i.
+  std::atomic<uint64_t> attr_done{0};
+};
+DeviceSlot g_devices[kMaxDevices];
+
+DeviceSlot* current_slot() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  DeviceSlot* slot = &g_devices[dev];
+  std::call_once(slot->once, [slot, dev] {
+    DeviceInfo info;
+    info.ordinal = dev;
+    cudaDeviceGetAttribute(&info.cc_major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&info.cc_minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cudaDeviceGetAttribute(&info.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&info.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    void* word = nullptr;
+    if (cudaGetSymbolAddress(&word, g_device_error_word) == cudaSuccess) {
+      info.error_word = static_cast<int*>(word);
+    }
+    slot->info = info;
+  });
+  return slot;
+}
+
+// Sets the dynamic shared memory limit of `kernel` once per device.
+template <typename Kernel>
+cudaError_t ensure_smem_attr(DeviceSlot* slot, int config_bit, Kernel kernel, int bytes) {
+  const uint64_t bit = uint64_t(1) << config_bit;
+  if (slot->attr_done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) slot->attr_done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
+
+template <typename T, int BN, int STAGES, bool KM>
+cudaError_t launch_umma_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit) {
+  using L = umma::Smem<BN, STAGES>;
+  CUtensorMap ta, tb, td;
+  const bool bf16 = a.bf16;
+  const bool b_ok = KM ? make_tma_2d(&tb, a.b, bf16, a.n, a.k, a.ldb, BN, umma::kBlockK, TmaSwizzle::B128)
+                       : make_tma_2d(&tb, a.b, bf16, a.k, a.n, a.ldb, umma::kBlockK, 64, TmaSwizzle::B128);
+  if (!b_ok ||
+      !make_tma_2d(&ta, a.a, bf16, a.m, a.k, a.lda, umma::kBlockM, umma::kBlockK, TmaSwizzle::B128) ||
+      !make_tma_2d(&td, a.d, bf16, a.m, a.n, a.ldd, 32, umma::kEpiCols, TmaSwizzle::B64)) {
+    return cudaErrorInvalidValue;
+  }
+  UmmaGemmParams p{};
+  p.m = static_cast<int>(a.m);
+  p.n = static_cast<int>(a.n);
+  p.k = static_cast<int>(a.k);
+  p.tiles_m = static_cast<int>((a.m + umma::kBlockM - 1) / umma::kBlockM);
+  p.tiles_n = static_cast<int>((a.n + BN - 1) / BN);
+  p.num_kb = static_cast<int>((a.k + umma::kBlockK - 1) / umma::kBlockK);
+  p.total_tiles = p.tiles_m * p.tiles_n;
+  p.group_m = std::min(p.tiles_m, 16);
+  p.alpha = a.alpha;
+  p.beta = a.beta;
+  p.c = a.c;
+  p.ldc = a.ldc;
+  p.bias = a.bias;
+  p.d = a.d;
+  p.ldd = a.ldd;
+  p.epi_flags = (a.beta != 0.0f ? kEpiHasC : 0u) | (a.bias != nullptr ? kEpiHasBias : 0u);
+  p.error_word = slot->info.error_word;
+
+  auto kernel = umma::gemm_kernel<T, BN, STAGES, KM>;
+  cudaError_t e = ensure_smem_attr(slot, config_bit, kernel, L::kDynamicBytes);
+  if (e != cudaSuccess) return e;
+  const int grid = std::min(p.total_tiles, slot->info.sm_count);
+  kernel<<<grid, umma::kThreads, L::kDynamicBytes, a.stream>>>(ta, tb, td, p);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return cudaGetLastError();
+}
+
+template <typename T, int MP, int STAGES, bool KM>
+cudaError_t launch_swapab_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit, int splits) {
+  using L = swapab::Smem<MP, STAGES>;
+  CUtensorMap tw, tx;
+  const bool bf16 = a.bf16;
+  // Weights: the B matrix ([K, N] row-major, or [N, K] when column-major);
+  // tokens: the A matrix [M, K].
+  const bool w_ok =
+      KM ? make_tma_2d(&tw, a.b, bf16, a.n, a.k, a.ldb, swapab::kBlockN, swapab::kBlockK, TmaSwizzle::B128)
+         : make_tma_2d(&tw, a.b, bf16, a.k, a.n, a.ldb, swapab::kBlockK, 64, TmaSwizzle::B128);
+  if (!w_ok ||
+      !make_tma_2d(&tx, a.a, bf16, a.m, a.k, a.lda, MP, swapab::kBlockK, TmaSwizzle::B128)) {
+    return cudaErrorInvalidValue;
+  }
+  SwapAbParams p{};
+  p.m = static_cast<int>(a.m);
+  p.n = static_cast<int>(a.n);
+  p.k = static_cast<int>(a.k);
+  p.num_kb = static_cast<int>((a.k + swapab::kBlockK - 1) / swapab::kBlockK);
+  p.splits = splits;
+  p.alpha = a.alpha;
+  p.beta = a.beta;
+  p.c = a.c;
+  p.ldc = a.ldc;
+  p.d = a.d;
+  p.ldd = a.ldd;
+  p.bias = a.bias;
+  p.epi_flags = (a.beta != 0.0f ? kEpiHasC : 0u) | (a.bias != nullptr ? kEpiHasBias : 0u);
+  p.error_word = slot->info.error_word;
+
+  auto kernel = swapab::gemm_kernel<T, MP, STAGES, KM>;
+  cudaError_t e = ensure_smem_attr(slot, config_bit, kernel, L::kDynamicBytes);
+  if (e != cudaSuccess) return e;
+
+  const int tiles_n = static_cast<int>((a.n + swapab::kBlockN - 1) / swapab::kBlockN);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(splits), static_cast<unsigned>(tiles_n), 1);
+  cfg.blockDim = dim3(swapab::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = L::kDynamicBytes;
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kernel, tw, tx, p);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_generic_t(const LaunchArgs& a) {
+  GenericGemmParams p{a.m,   a.n,   a.k,   a.a,     a.lda,  a.b,   a.ldb,
+                      a.c,   a.ldc, a.d,   a.ldd,   a.bias, a.alpha, a.beta,
+                      a.b_col_major ? 1 : 0};
+  const int64_t tiles_n = (a.n + generic::kTile - 1) / generic::kTile;
+  const int64_t tiles_m = (a.m + generic::kTile - 1) / generic::kTile;
+  if (tiles_n > 2147483647LL) return cudaErrorInvalidValue;
+  const dim3 grid(static_cast<unsigned>(tiles_n), static_cast<unsigned>(std::min<int64_t>(tiles_m, 65535)));
+  generic::gemm_kernel<T><<<grid, generic::kThreads, 0, a.stream>>>(p);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return cudaGetLastError();
+}
+
+// Kernel configuration bits for ensure_smem_attr: one per instantiation,
+// the column-major-B variant of configuration c uses bit c + kCfgColMajorB.
+enum : int {
+  kCfgUmmaBf16N256 = 0,
+  kCfgUmmaF16N256,
+  kCfgUmmaBf16N128,
+  kCfgUmmaF16N128,
+  kCfgSwapBf16M16,
+  kCfgSwapF16M16,
+  kCfgSwapBf16M32,
+  kCfgSwapF16M32,
+  kCfgSwapBf16M64,
+  kCfgSwapF16M64,
+  kCfgColMajorB = 16,
+};
+
+template <bool KM>
+cudaError_t launch_umma_km(const LaunchArgs& a, DeviceSlot* slot, int bn) {
+  const int off = KM ? kCfgColMajorB : 0;
+  if (bn == 256) {
+    return a.bf16 ? launch_umma_t<__nv_bfloat16, 256, 4, KM>(a, slot, kCfgUmmaBf16N256 + off)
+                  : launch_umma_t<half, 256, 4, KM>(a, slot, kCfgUmmaF16N256 + off);
+  }
+  return a.bf16 ? launch_umma_t<__nv_bfloat16, 128, 6, KM>(a, slot, kCfgUmmaBf16N128 + off)
+                : launch_umma_t<half, 128, 6, KM>(a, slot, kCfgUmmaF16N128 + off);
+}
+
+template <bool KM>
+cudaError_t launch_swapab_km(const LaunchArgs& a, DeviceSlot* slot, int splits) {
+  const int off = KM ? kCfgColMajorB : 0;
+  if (a.m <= 16) {
+    return a.bf16 ? launch_swapab_t<__nv_bfloat16, 16, 10, KM>(a, slot, kCfgSwapBf16M16 + off, splits)
+                  : launch_swapab_t<half, 16, 10, KM>(a, slot, kCfgSwapF16M16 + off, splits);
+  }
+  if (a.m <= 32) {
+    return a.bf16 ? launch_swapab_t<__nv_bfloat16, 32, 9, KM>(a, slot, kCfgSwapBf16M32 + off, splits)
+                  : launch_swapab_t<half, 32, 9, KM>(a, slot, kCfgSwapF16M32 + off, splits);
+  }
+  return a.bf16 ? launch_swapab_t<__nv_bfloat16, 64, 7, KM>(a, slot, kCfgSwapBf16M64 + off, splits)
+                : launch_swapab_t<half, 64, 7, KM>(a, slot, kCfgSwapF16M64 + off, splits);
+}
+
+}  // namespace
+
+const DeviceInfo* current_device_info() {
+  DeviceSlot* slot = current_slot();
+  return slot ? &slot->info : nullptr;
+}
+
+int umma_choose_bn(int64_t m, int64_t n, int sm_count) {
+  // Prefer 128x256 tiles; fall back to 128x128 when 256-wide tiles would
+  // leave most SMs idle (small problems) or N itself is narrow.
+  if (n <= 128) return 128;
+  const int64_t tiles_256 = ((m + 127) / 128) * ((n + 255) / 256);
+  if (tiles_256 < sm_count / 2) return 128;
+  return 256;
+}
+
+int swapab_choose_splits(int64_t n, int64_t k, int sm_count) {
+  const int64_t tiles_n = (n + swapab::kBlockN - 1) / swapab::kBlockN;
+  const int64_t num_kb = (k + swapab::kBlockK - 1) / swapab::kBlockK;
+  int64_t s = sm_count / std::max<int64_t>(tiles_n, 1);
+  s = std::min<int64_t>(s, 8);
+  s = std::min<int64_t>(s, num_kb);
+  return static_cast<int>(std::max<int64_t>(s, 1));
+}
+
+cudaError_t launch_umma_gemm(const LaunchArgs& a, int bn) {
+  DeviceSlot* slot = current_slot();
+  if (slot == nullptr) return cudaErrorInvalidDevice;
+  return a.b_col_major ? launch_umma_km<true>(a, slot, bn) : launch_umma_km<false>(a, slot, bn);
+}
+
+cudaError_t launch_umma_swapab_gemm(const LaunchArgs& a, int* splits_used) {
+  DeviceSlot* slot = current_slot();
+  if (slot == nullptr) return cudaErrorInvalidDevice;
+  const int splits = swapab_choose_splits(a.n, a.k, slot->info.sm_count);
+  if (splits_used) *splits_used = splits;
+  return a.b_col_major ? launch_swapab_km<true>(a, slot, splits) : launch_swapab_km<false>(a, slot, splits);
+}
+
+cudaError_t launch_generic_gemm(const LaunchArgs& a) {
+  return a.bf16 ? launch_generic_t<__nv_bfloat16>(a) : launch_generic_t<half>(a);
+}
+
+int read_and_clear_error_word(bool clear) {
+  int value = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  if (cudaMemcpyFromSymbol(&value, g_device_error_word, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && value != 0) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_device_error_word, &zero, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return value;
+}
+
+uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
+
+}  // namespace zcb

@@ -1,0 +1,53 @@
+// Kernel launchers: the only place that turns host arguments into CUDA
+// launches. Everything here assumes the arguments already passed validation.
+#pragma once
+
+#include <cstdint>
+
+#include <cuda_runtime_api.h>
+
+namespace zcb {
+
+struct LaunchArgs {
+  int64_t m, n, k;
+  const void* a;
+  int64_t lda;
+  const void* b;
+  int64_t ldb;
+  const void* c;  // null when beta == 0
+  int64_t ldc;
+  void* d;
+  int64_t ldd;
+  const void* bias;
+  float alpha, beta;
+  bool bf16;
+  bool b_col_major;  // B[k][n] at n*ldb + k (PyTorch [N, K] weight)
+  cudaStream_t stream;
+};
+
+// Per-device facts, cached on first use.
+struct DeviceInfo {
+  int ordinal = -1;
+  int cc_major = 0, cc_minor = 0;
+  int sm_count = 0;
+  int max_smem_optin = 0;
+  int* error_word = nullptr;  // device address of this device's error word
+};
+const DeviceInfo* current_device_info();
+
+// Persistent tcgen05 kernel, 128 x bn tiles (bn in {128, 256}).
+cudaError_t launch_umma_gemm(const LaunchArgs& args, int bn);
+// Swap-AB tcgen05 kernel for small M (M <= 32): split-K across a thread-block
+// cluster, reduced through distributed shared memory.
+cudaError_t launch_umma_swapab_gemm(const LaunchArgs& args, int* splits_used);
+// Predicated CUDA-core kernel for TMA-incompatible layouts.
+cudaError_t launch_generic_gemm(const LaunchArgs& args);
+
+// Shape heuristics shared by dispatch and telemetry.
+int umma_choose_bn(int64_t m, int64_t n, int sm_count);
+int swapab_choose_splits(int64_t n, int64_t k, int sm_count);
+
+int read_and_clear_error_word(bool clear);
+uint64_t launch_count();
+
+}  // namespace zcb
