@@ -58,6 +58,7 @@ def test_rowmajor_entry_point(cuda_device):
 # ---------------------------------------------------------------- forced families
 
 FAMILIES = {
+    "pair256": "_256x256x64_2cta_persistent",
     "persistent256": "_128x256x64_ws_persistent",
     "persistent128": "_128x128x64_ws_persistent",
     "swapab16": "_16x128x64_swapab",
@@ -68,6 +69,8 @@ FAMILIES = {
 
 # (m, n, k) per family: ragged edges in every dimension, K tails, multi-tile.
 FAMILY_SHAPES = {
+    # (300, ...): the second tile row's follower CTA (rows 384..511) lies wholly outside M.
+    "pair256": [(256, 256, 64), (300, 520, 200), (1000, 777, 1032), (2048, 4096, 1024), (4096, 1536, 8960)],
     "persistent256": [(128, 256, 64), (300, 520, 200), (1000, 777, 1032), (2048, 4096, 1024)],
     "persistent128": [(128, 128, 64), (129, 136, 72), (513, 1000, 520), (1536, 2048, 1536)],
     "swapab16": [(1, 128, 128), (7, 300, 200), (16, 1000, 4096), (13, 4096, 1032)],

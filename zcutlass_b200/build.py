@@ -28,6 +28,7 @@ INCLUDE = ROOT / "include"
 BUILD = PKG / "_build"
 CORE_SO = PKG / "libzcutlass.so"
 TORCH_SO = PKG / "libzcutlass_torch.so"
+BENCH_BIN = PKG / "zcutlass_bench"
 
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 NVCC = str(CUDA_HOME / "bin" / "nvcc")
@@ -99,6 +100,17 @@ def build_torch_ops(verbose: bool = False) -> Path:
     return TORCH_SO
 
 
+def build_bench(verbose: bool = False) -> Path:
+    """zcutlass_b200/zcutlass_bench: the native benchmark (cuBLAS as comparator)."""
+    build_core(verbose)
+    src = CSRC / "bin" / "bench_gemm.cpp"
+    if _stale(BENCH_BIN, [src, CORE_SO, *_headers()]):
+        _run([CXX, "-std=c++17", "-O2", "-o", str(BENCH_BIN), str(src), f"-I{INCLUDE}",
+              f"-I{CUDA_HOME / 'include'}", f"-L{PKG}", "-lzcutlass", f"-L{CUDA_HOME / 'lib64'}",
+              "-lcublas", "-lcudart", "-Wl,-rpath,$ORIGIN"], verbose)
+    return BENCH_BIN
+
+
 def build_oracle(verbose: bool = False) -> None:
     """Builds oracle/liboracle.so and, when the reference sources exist,
     oracle/_ref/libzcutlass_ref.so (test infrastructure only)."""
@@ -115,6 +127,7 @@ def build_oracle(verbose: bool = False) -> None:
 def build_all(oracle: bool = True, verbose: bool = False) -> None:
     build_core(verbose)
     build_torch_ops(verbose)
+    build_bench(verbose)
     if oracle:
         build_oracle(verbose)
 

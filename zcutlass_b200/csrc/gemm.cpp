@@ -127,7 +127,7 @@ SelectDevice select_device() {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-enum class Kind { UmmaPersistent, UmmaSwapAb, Generic };
+enum class Kind { UmmaPair, UmmaPersistent, UmmaSwapAb, Generic };
 
 class Sm100Operation final : public GemmOperation {
  public:
@@ -184,7 +184,10 @@ class Sm100Operation final : public GemmOperation {
     if (!zcb::tma_compatible(args.D.data, args.D.ld)) return false;
     if (args.beta != 0.0f && (!aligned16(args.C.data) || (args.C.ld & 7) != 0)) return false;
     if (args.bias != nullptr && !aligned16(args.bias)) return false;
-    return forced || zcb::umma_choose_bn(m, n, dev.sm_count) == desc_.tile_n;
+    if (forced) return true;
+    const zcb::PersistentConfig want = zcb::choose_persistent(m, n, dev.sm_count);
+    if (kind_ == Kind::UmmaPair) return want == zcb::PersistentConfig::Pair256x256;
+    return want == (desc_.tile_n == 256 ? zcb::PersistentConfig::Cta128x256 : zcb::PersistentConfig::Cta128x128);
   }
 
   Status run(const GemmArguments& args, const GemmPreference&) const override {
@@ -208,6 +211,9 @@ class Sm100Operation final : public GemmOperation {
     la.stream = args.stream;
     cudaError_t e = cudaSuccess;
     switch (kind_) {
+      case Kind::UmmaPair:
+        e = zcb::launch_umma_pair_gemm(la);
+        break;
       case Kind::UmmaPersistent:
         e = zcb::launch_umma_gemm(la, desc_.tile_n);
         break;
@@ -234,8 +240,9 @@ void register_builtin_operations() {
   using F = ShapeFamily;
   using E = EpilogueKind;
   // First match wins: small-M swap-AB buckets, then the persistent kernels
-  // (256- or 128-wide tiles, whichever umma_choose_bn picks), then the
-  // predicated CUDA-core kernel that accepts any row-major layout.
+  // (CTA-pair 256x256, or one-CTA 128x256 / 128x128 tiles, whichever the
+  // wave-quantisation model in choose_persistent picks), then the predicated
+  // CUDA-core kernel that accepts any layout.
   static const Sm100Operation ops[] = {
       {"zcutlass_sm100_tcgen05_bf16_16x128x64_swapab_splitk", DType::BF16, K::UmmaSwapAb, 16, 128, 64, 10, F::Decode, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_f16_16x128x64_swapab_splitk", DType::F16, K::UmmaSwapAb, 16, 128, 64, 10, F::Decode, E::RegisterLinear},
@@ -243,6 +250,8 @@ void register_builtin_operations() {
       {"zcutlass_sm100_tcgen05_f16_32x128x64_swapab_splitk", DType::F16, K::UmmaSwapAb, 32, 128, 64, 9, F::Decode, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_bf16_64x128x64_swapab_splitk", DType::BF16, K::UmmaSwapAb, 64, 128, 64, 7, F::Prefill, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_f16_64x128x64_swapab_splitk", DType::F16, K::UmmaSwapAb, 64, 128, 64, 7, F::Prefill, E::RegisterLinear},
+      {"zcutlass_sm100_tcgen05_bf16_256x256x64_2cta_persistent", DType::BF16, K::UmmaPair, 256, 256, 64, 6, F::Large, E::TmemRegisterTma},
+      {"zcutlass_sm100_tcgen05_f16_256x256x64_2cta_persistent", DType::F16, K::UmmaPair, 256, 256, 64, 6, F::Large, E::TmemRegisterTma},
       {"zcutlass_sm100_tcgen05_bf16_128x256x64_ws_persistent", DType::BF16, K::UmmaPersistent, 128, 256, 64, 4, F::Large, E::TmemRegisterTma},
       {"zcutlass_sm100_tcgen05_f16_128x256x64_ws_persistent", DType::F16, K::UmmaPersistent, 128, 256, 64, 4, F::Large, E::TmemRegisterTma},
       {"zcutlass_sm100_tcgen05_bf16_128x128x64_ws_persistent", DType::BF16, K::UmmaPersistent, 128, 128, 64, 6, F::Prefill, E::TmemRegisterTma},

@@ -110,6 +110,17 @@ __device__ __forceinline__ void load_row_chunk(const T* src, int valid, float (&
   }
 }
 
+// Stores the first `valid` (< 32) of 32 packed 16-bit values to dst; fully
+// unrolled so `packed` stays in registers.
+template <typename T>
+__device__ __forceinline__ void store_row_prefix(T* dst, const uint32_t (&packed)[16], int valid) {
+  uint16_t* d = reinterpret_cast<uint16_t*>(dst);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    if (i < valid) d[i] = static_cast<uint16_t>((i & 1) ? (packed[i >> 1] >> 16) : (packed[i >> 1] & 0xffffu));
+  }
+}
+
 // kBKMajor: B is given column-major (B[k][n] at n*ldb + k, i.e. a PyTorch
 // [N, K] weight); its tiles are then K-major like A's.
 template <typename T, int BN, int STAGES, bool kBKMajor>
@@ -302,12 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // Ragged last chunk: a TMA store clips the inner dimension in 16-byte
           // units, which would touch D's padding columns when N is not a
           // multiple of 8. Store exactly the in-bounds elements instead.
-          if (row_ok) {
-            const uint16_t* h = reinterpret_cast<const uint16_t*>(packed);
-            uint16_t* drow = reinterpret_cast<uint16_t*>(static_cast<T*>(p.d) + static_cast<int64_t>(row) * p.ldd + nc);
-            const int valid = p.n - nc;
-            for (int i = 0; i < valid; ++i) drow[i] = h[i];
-          }
+          if (row_ok) store_row_prefix(static_cast<T*>(p.d) + static_cast<int64_t>(row) * p.ldd + nc, packed, p.n - nc);
           continue;
         }
         uint8_t* sb = stage_base + (chunk_ctr & 1u) * L::kEpiBufBytes;

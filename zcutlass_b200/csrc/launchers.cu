@@ -7,6 +7,7 @@
 
 #include "kernels/generic_gemm.cuh"
 #include "kernels/sm100_umma_gemm.cuh"
+#include "kernels/sm100_umma_gemm_2cta.cuh"
 #include "kernels/sm100_umma_swapab.cuh"
 #include "tma_desc.hpp"
 
@@ -26,6 +27,8 @@ struct DeviceSlot {
   DeviceInfo info;
   // Bit i set once cudaFuncSetAttribute ran for kernel configuration i.
   std::atomic<uint64_t> attr_done{0};
+  // Resident CTA pairs of each cluster-launched configuration (0 = not queried).
+  int max_active_pairs[64] = {};
 };
 DeviceSlot g_devices[kMaxDevices];
 
@@ -152,6 +155,70 @@ cudaError_t launch_swapab_t(const LaunchArgs& a, DeviceSlot* slot, int config_bi
   return cudaGetLastError();
 }
 
+template <typename T, int STAGES, bool KM>
+cudaError_t launch_umma2_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit) {
+  using L = umma2::Smem<STAGES>;
+  CUtensorMap ta, tb, td;
+  const bool bf16 = a.bf16;
+  const bool b_ok =
+      KM ? make_tma_2d(&tb, a.b, bf16, a.n, a.k, a.ldb, umma2::kHalfN, umma2::kBlockK, TmaSwizzle::B128)
+         : make_tma_2d(&tb, a.b, bf16, a.k, a.n, a.ldb, umma2::kBlockK, 64, TmaSwizzle::B128);
+  if (!b_ok ||
+      !make_tma_2d(&ta, a.a, bf16, a.m, a.k, a.lda, umma2::kHalfM, umma2::kBlockK, TmaSwizzle::B128) ||
+      !make_tma_2d(&td, a.d, bf16, a.m, a.n, a.ldd, 32, umma2::kEpiCols, TmaSwizzle::B64)) {
+    return cudaErrorInvalidValue;
+  }
+  UmmaGemmParams p{};
+  p.m = static_cast<int>(a.m);
+  p.n = static_cast<int>(a.n);
+  p.k = static_cast<int>(a.k);
+  p.tiles_m = static_cast<int>((a.m + umma2::kBlockM - 1) / umma2::kBlockM);
+  p.tiles_n = static_cast<int>((a.n + umma2::kBlockN - 1) / umma2::kBlockN);
+  p.num_kb = static_cast<int>((a.k + umma2::kBlockK - 1) / umma2::kBlockK);
+  p.total_tiles = p.tiles_m * p.tiles_n;
+  p.group_m = std::min(p.tiles_m, 8);
+  p.alpha = a.alpha;
+  p.beta = a.beta;
+  p.c = a.c;
+  p.ldc = a.ldc;
+  p.bias = a.bias;
+  p.d = a.d;
+  p.ldd = a.ldd;
+  p.epi_flags = (a.beta != 0.0f ? kEpiHasC : 0u) | (a.bias != nullptr ? kEpiHasBias : 0u);
+  p.error_word = slot->info.error_word;
+
+  auto kernel = umma2::gemm_kernel<T, STAGES, KM>;
+  cudaError_t e = ensure_smem_attr(slot, config_bit, kernel, L::kDynamicBytes);
+  if (e != cudaSuccess) return e;
+
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(umma2::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = L::kDynamicBytes;
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // Persistent grid: as many CTA pairs as can be resident at once (queried
+  // once per device), never more than there are tiles.
+  int& max_pairs = slot->max_active_pairs[config_bit];
+  if (max_pairs == 0) {
+    cfg.gridDim = dim3(static_cast<unsigned>(slot->info.sm_count & ~1), 1, 1);
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters <= 0)
+      clusters = slot->info.sm_count / 2;
+    max_pairs = clusters;
+  }
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * std::min(p.total_tiles, max_pairs)), 1, 1);
+  e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, td, p);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
 template <typename T>
 cudaError_t launch_generic_t(const LaunchArgs& a) {
   GenericGemmParams p{a.m,   a.n,   a.k,   a.a,     a.lda,  a.b,   a.ldb,
@@ -179,6 +246,8 @@ enum : int {
   kCfgSwapF16M32,
   kCfgSwapBf16M64,
   kCfgSwapF16M64,
+  kCfgPairBf16,
+  kCfgPairF16,
   kCfgColMajorB = 16,
 };
 
@@ -215,13 +284,34 @@ const DeviceInfo* current_device_info() {
   return slot ? &slot->info : nullptr;
 }
 
-int umma_choose_bn(int64_t m, int64_t n, int sm_count) {
-  // Prefer 128x256 tiles; fall back to 128x128 when 256-wide tiles would
-  // leave most SMs idle (small problems) or N itself is narrow.
-  if (n <= 128) return 128;
-  const int64_t tiles_256 = ((m + 127) / 128) * ((n + 255) / 256);
-  if (tiles_256 < sm_count / 2) return 128;
-  return 256;
+PersistentConfig choose_persistent(int64_t m, int64_t n, int sm_count) {
+  // Wave-quantisation cost model: time ~ waves * per-SM tile area / relative
+  // efficiency, where a wave is one tile per SM (one 256x256 tile per CTA
+  // pair). Efficiencies are the measured throughput ratios of the kernels on
+  // large problems (pair 256x256 : 128x256 : 128x128).
+  struct Cand {
+    PersistentConfig cfg;
+    int tile_m, tile_n, units;
+    double per_sm_area, eff;
+  };
+  const int pairs = sm_count / 2;
+  const Cand cands[] = {
+      {PersistentConfig::Pair256x256, 256, 256, pairs, 256.0 * 256.0 / 2.0, 1.0},
+      {PersistentConfig::Cta128x256, 128, 256, sm_count, 128.0 * 256.0, 0.86},
+      {PersistentConfig::Cta128x128, 128, 128, sm_count, 128.0 * 128.0, 0.72},
+  };
+  PersistentConfig best = PersistentConfig::Cta128x128;
+  double best_cost = 1e300;
+  for (const Cand& c : cands) {
+    const int64_t tiles = ((m + c.tile_m - 1) / c.tile_m) * ((n + c.tile_n - 1) / c.tile_n);
+    const int64_t waves = (tiles + c.units - 1) / c.units;
+    const double cost = static_cast<double>(waves) * c.per_sm_area / c.eff;
+    if (cost < best_cost * 0.999) {
+      best_cost = cost;
+      best = c.cfg;
+    }
+  }
+  return best;
 }
 
 int swapab_choose_splits(int64_t n, int64_t k, int sm_count) {
@@ -237,6 +327,18 @@ cudaError_t launch_umma_gemm(const LaunchArgs& a, int bn) {
   DeviceSlot* slot = current_slot();
   if (slot == nullptr) return cudaErrorInvalidDevice;
   return a.b_col_major ? launch_umma_km<true>(a, slot, bn) : launch_umma_km<false>(a, slot, bn);
+}
+
+cudaError_t launch_umma_pair_gemm(const LaunchArgs& a) {
+  DeviceSlot* slot = current_slot();
+  if (slot == nullptr) return cudaErrorInvalidDevice;
+  const int off = a.b_col_major ? kCfgColMajorB : 0;
+  if (a.b_col_major) {
+    return a.bf16 ? launch_umma2_t<__nv_bfloat16, 6, true>(a, slot, kCfgPairBf16 + off)
+                  : launch_umma2_t<half, 6, true>(a, slot, kCfgPairF16 + off);
+  }
+  return a.bf16 ? launch_umma2_t<__nv_bfloat16, 6, false>(a, slot, kCfgPairBf16 + off)
+                : launch_umma2_t<half, 6, false>(a, slot, kCfgPairF16 + off);
 }
 
 cudaError_t launch_umma_swapab_gemm(const LaunchArgs& a, int* splits_used) {

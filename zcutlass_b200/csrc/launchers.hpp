@@ -37,6 +37,8 @@ const DeviceInfo* current_device_info();
 
 // Persistent tcgen05 kernel, 128 x bn tiles (bn in {128, 256}).
 cudaError_t launch_umma_gemm(const LaunchArgs& args, int bn);
+// Persistent tcgen05 kernel on CTA pairs (cta_group::2), 256 x 256 tiles.
+cudaError_t launch_umma_pair_gemm(const LaunchArgs& args);
 // Swap-AB tcgen05 kernel for small M (M <= 32): split-K across a thread-block
 // cluster, reduced through distributed shared memory.
 cudaError_t launch_umma_swapab_gemm(const LaunchArgs& args, int* splits_used);
@@ -44,7 +46,8 @@ cudaError_t launch_umma_swapab_gemm(const LaunchArgs& args, int* splits_used);
 cudaError_t launch_generic_gemm(const LaunchArgs& args);
 
 // Shape heuristics shared by dispatch and telemetry.
-int umma_choose_bn(int64_t m, int64_t n, int sm_count);
+enum class PersistentConfig { Pair256x256, Cta128x256, Cta128x128 };
+PersistentConfig choose_persistent(int64_t m, int64_t n, int sm_count);
 int swapab_choose_splits(int64_t n, int64_t k, int sm_count);
 
 int read_and_clear_error_word(bool clear);
