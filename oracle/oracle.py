@@ -95,7 +95,8 @@ def float_to_bits(x: np.ndarray, dtype: int) -> np.ndarray:
     """Round-to-nearest-even narrowing of float32 to f16/bf16 bit patterns."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     if dtype == F16:
-        return x.astype(np.float16).view(np.uint16)
+        with np.errstate(over="ignore"):  # values beyond the f16 range become inf, as in the kernels
+            return x.astype(np.float16).view(np.uint16)
     u = x.view(np.uint32).astype(np.uint64)
     nan = (u & 0x7FFFFFFF) > 0x7F800000
     r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)

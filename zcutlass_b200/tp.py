@@ -13,8 +13,9 @@ vLLM. This module provides the same two shardings natively:
       chunks so the all-reduce of chunk i overlaps the GEMM of chunk i+1.
 
 Weights use the PyTorch [out_features, in_features] layout and go to the
-kernels as column-major B (no transposed copy). All GEMMs run through
-torch.ops.zcutlass.gemm_out on the current stream.
+kernels as column-major B (no transposed copy). Every GEMM runs through the
+zcutlass C ABI (zcutlass_gemm) on the current stream; `linear_fn` replaces
+that call only in tests that check the sharding logic on CPU ranks.
 """
 
 from __future__ import annotations
@@ -67,23 +68,24 @@ def _linear_into(x, weight, bias, out) -> None:
 class ColumnParallelLinear:
     """y_shard = x @ W_shard^T + b_shard; W_shard = W[rows owned by this rank]."""
 
-    def __init__(self, weight_shard, bias_shard=None, tp: TPGroup | None = None) -> None:
+    def __init__(self, weight_shard, bias_shard=None, tp: TPGroup | None = None, linear_fn=None) -> None:
         self.weight = weight_shard
         self.bias = bias_shard
         self.tp = tp or TPGroup()
+        self.linear_fn = linear_fn or _linear_into
 
     @classmethod
-    def from_full(cls, weight, bias=None, tp: TPGroup | None = None) -> "ColumnParallelLinear":
+    def from_full(cls, weight, bias=None, tp: TPGroup | None = None, linear_fn=None) -> "ColumnParallelLinear":
         tp = tp or TPGroup()
         lo, hi = shard_range(weight.shape[0], tp.rank, tp.world_size)
-        return cls(weight[lo:hi].contiguous(), None if bias is None else bias[lo:hi].contiguous(), tp)
+        return cls(weight[lo:hi].contiguous(), None if bias is None else bias[lo:hi].contiguous(), tp, linear_fn)
 
     def forward(self, x, out=None):
         import torch
 
         if out is None:
             out = torch.empty(x.shape[0], self.weight.shape[0], device=x.device, dtype=x.dtype)
-        _linear_into(x, self.weight, self.bias, out)
+        self.linear_fn(x, self.weight, self.bias, out)
         return out
 
     __call__ = forward
@@ -95,17 +97,20 @@ class RowParallelLinear:
     The bias is added once, by rank 0's partial, so the all-reduced sum carries
     it exactly once. `chunks` row blocks let NCCL overlap with the GEMM."""
 
-    def __init__(self, weight_shard, bias=None, tp: TPGroup | None = None, chunks: int = 4) -> None:
+    def __init__(self, weight_shard, bias=None, tp: TPGroup | None = None, chunks: int = 4,
+                 linear_fn=None) -> None:
         self.weight = weight_shard
         self.bias = bias
         self.tp = tp or TPGroup()
         self.chunks = max(1, chunks)
+        self.linear_fn = linear_fn or _linear_into
 
     @classmethod
-    def from_full(cls, weight, bias=None, tp: TPGroup | None = None, chunks: int = 4) -> "RowParallelLinear":
+    def from_full(cls, weight, bias=None, tp: TPGroup | None = None, chunks: int = 4,
+                  linear_fn=None) -> "RowParallelLinear":
         tp = tp or TPGroup()
         lo, hi = shard_range(weight.shape[1], tp.rank, tp.world_size)
-        return cls(weight[:, lo:hi].contiguous(), bias, tp, chunks)
+        return cls(weight[:, lo:hi].contiguous(), bias, tp, chunks, linear_fn)
 
     def forward(self, x_shard, out=None):
         import torch
@@ -116,7 +121,7 @@ class RowParallelLinear:
             out = torch.empty(m, self.weight.shape[0], device=x_shard.device, dtype=x_shard.dtype)
         bias = self.bias if self.tp.rank == 0 else None
         if self.tp.world_size == 1:
-            _linear_into(x_shard, self.weight, bias, out)
+            self.linear_fn(x_shard, self.weight, bias, out)
             return out
         works = []
         chunks = min(self.chunks, m)
@@ -124,7 +129,7 @@ class RowParallelLinear:
             r0, r1 = shard_range(m, i, chunks)
             if r1 == r0:
                 continue
-            _linear_into(x_shard[r0:r1], self.weight, bias, out[r0:r1])
+            self.linear_fn(x_shard[r0:r1], self.weight, bias, out[r0:r1])
             works.append(dist.all_reduce(out[r0:r1], op=dist.ReduceOp.SUM, group=self.tp.group, async_op=True))
         for w in works:
             w.wait()
@@ -171,7 +176,7 @@ class TPDecoderLinears:
     """
 
     def __init__(self, shape: LayerShape, tp: TPGroup, device, dtype, seed: int = 0, chunks: int = 4,
-                 qkv_bias: bool = False) -> None:
+                 qkv_bias: bool = False, linear_fn=None) -> None:
         import torch
 
         self.shape, self.tp = shape, tp
@@ -187,10 +192,10 @@ class TPDecoderLinears:
         o_lo, o_hi = shard_range(shape.o_in, tp.rank, w)
         d_lo, d_hi = shard_range(inter, tp.rank, w)
         self.qkv = ColumnParallelLinear(rnd(qkv_hi - qkv_lo, h, scale=h ** -0.5),
-                                        rnd(qkv_hi - qkv_lo, scale=0.1) if qkv_bias else None, tp)
-        self.gate_up = ColumnParallelLinear(rnd(gu_hi - gu_lo, h, scale=h ** -0.5), None, tp)
-        self.o_proj = RowParallelLinear(rnd(h, o_hi - o_lo, scale=shape.o_in ** -0.5), None, tp, chunks)
-        self.down = RowParallelLinear(rnd(h, d_hi - d_lo, scale=inter ** -0.5), None, tp, chunks)
+                                        rnd(qkv_hi - qkv_lo, scale=0.1) if qkv_bias else None, tp, linear_fn)
+        self.gate_up = ColumnParallelLinear(rnd(gu_hi - gu_lo, h, scale=h ** -0.5), None, tp, linear_fn)
+        self.o_proj = RowParallelLinear(rnd(h, o_hi - o_lo, scale=shape.o_in ** -0.5), None, tp, chunks, linear_fn)
+        self.down = RowParallelLinear(rnd(h, d_hi - d_lo, scale=inter ** -0.5), None, tp, chunks, linear_fn)
         self.o_cols = o_hi - o_lo
         self.d_cols = d_hi - d_lo
         self._bufs = {}
