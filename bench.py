@@ -295,6 +295,10 @@ def run_gpu(args) -> int:
     gate_flops = 2.0 * TOKENS * layer.gate_up.weight.shape[0] * layer.gate_up.weight.shape[1]
     gate_tflops = gate_flops / (gate_ms * 1e-3) / 1e12
     peak = peaks["bf16_tflops_sustained"]
+    gw = layer.gate_up.weight
+    gate_kernel = _native.selected_kernel(_native.make_desc(
+        TOKENS, gw.shape[0], gw.shape[1], gw.shape[1], gw.shape[1], gw.shape[0], gw.shape[0], _native.BF16,
+        b_layout=_native.COLUMN_MAJOR))["kernel_name"]
 
     # ---- end to end through the C ABI with pinned host buffers
     e2e = run_e2e(args, layer, x_host, device, barrier, max_over_ranks, total_flops)
@@ -315,7 +319,7 @@ def run_gpu(args) -> int:
             "config": cfg,
             "per_gpu_tflops": round(value / world, 2),
             "frac_of_bf16_peak_per_gpu": round(value / world / peak, 4),
-            "roofline": {"bound": "tensor", "kernel": "gate_up (zcutlass_sm100_tcgen05_bf16_128x256x64_ws_persistent)",
+            "roofline": {"bound": "tensor", "kernel": f"gate_up ({gate_kernel})",
                          "achieved": round(gate_tflops, 2), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(gate_tflops / peak, 4),
                          "peak_source": f"bf16_tflops_sustained of {peaks_src} (burst {peaks['bf16_tflops']})",

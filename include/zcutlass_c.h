@@ -22,6 +22,7 @@
  *   zcutlass_device_error       read/clear the device-side error word that the
  *                               tcgen05 kernels set when a bounded wait expires
  *   zcutlass_gemm_kernel_launches  number of kernel launches this library made
+ *   zcutlass_selftest_bounded_wait runs a kernel whose bounded wait must expire
  *
  * Integer enum values equal the C++ enum values (Status, DType, LayoutKind).
  * Return values of type int that carry a status use zcutlass_status values.
@@ -107,6 +108,13 @@ int zcutlass_device_error(int clear);
 
 /* Number of kernel launches this library has enqueued since load (all devices). */
 uint64_t zcutlass_gemm_kernel_launches(void);
+
+/* Failure-detection self test (no reference counterpart): launches one kernel
+ * whose bounded mbarrier wait is never satisfied, with a limit of `timeout_us`
+ * microseconds. The wait gives up, records an error code and the kernel
+ * returns; the call synchronises and returns that code (non-zero), clearing
+ * the error word, or -1 if CUDA itself failed. The device stays usable. */
+int zcutlass_selftest_bounded_wait(uint32_t timeout_us);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -87,6 +87,7 @@ SIGNATURES = {
     "zcutlass_version_patch": (ctypes.c_int, []),
     "zcutlass_device_error": (ctypes.c_int, [ctypes.c_int]),
     "zcutlass_gemm_kernel_launches": (ctypes.c_uint64, []),
+    "zcutlass_selftest_bounded_wait": (ctypes.c_int, [ctypes.c_uint32]),
 }
 
 _LIB: ctypes.CDLL | None = None

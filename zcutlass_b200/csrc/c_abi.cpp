@@ -115,4 +115,6 @@ int zcutlass_device_error(int clear) { return zcb::read_and_clear_error_word(cle
 
 uint64_t zcutlass_gemm_kernel_launches(void) { return zcb::launch_count(); }
 
+int zcutlass_selftest_bounded_wait(uint32_t timeout_us) { return zcb::selftest_bounded_wait(timeout_us); }
+
 }  // extern "C"

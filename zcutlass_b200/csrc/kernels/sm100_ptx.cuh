@@ -72,6 +72,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 struct WaitCtx {
   volatile int* abort_flag;  // shared
   int* error_word;           // global, may be null
+  uint64_t timeout_ns = kWaitTimeoutNs;
 };
 
 __device__ __noinline__ void report_wait_timeout(const WaitCtx& ctx, int code) {
@@ -90,7 +91,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
     if (mbar_try_wait(addr, parity)) return true;
     if ((spin & 255u) == 0u) {
       if (*ctx.abort_flag) return false;
-      if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+      if (global_timer_ns() - t0 > ctx.timeout_ns) {
         report_wait_timeout(ctx, code);
         return false;
       }

@@ -366,4 +366,30 @@ int read_and_clear_error_word(bool clear) {
 
 uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
+// One thread waits on an mbarrier that nothing ever arrives on, with the same
+// bounded wait the GEMM kernels use but a caller-chosen limit. The wait must
+// give up, record kSelftestCode in the error word and let the kernel return.
+constexpr int kSelftestCode = (15 << 4) | 15;
+
+__global__ void selftest_bounded_wait_kernel(uint64_t timeout_ns, int* error_word) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  abort_flag = 0;
+  fence_mbarrier_init();
+  WaitCtx ctx{&abort_flag, error_word, timeout_ns};
+  (void)mbar_wait(&bar, 0, ctx, kSelftestCode);
+}
+
+int selftest_bounded_wait(uint32_t timeout_us) {
+  DeviceSlot* slot = current_slot();
+  if (slot == nullptr || slot->info.error_word == nullptr) return -1;
+  if (read_and_clear_error_word(true) < 0) return -1;
+  selftest_bounded_wait_kernel<<<1, 32>>>(static_cast<uint64_t>(timeout_us) * 1000ull, slot->info.error_word);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  if (cudaGetLastError() != cudaSuccess) return -1;
+  return read_and_clear_error_word(true);
+}
+
 }  // namespace zcb

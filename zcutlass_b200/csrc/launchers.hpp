@@ -51,6 +51,9 @@ PersistentConfig choose_persistent(int64_t m, int64_t n, int sm_count);
 int swapab_choose_splits(int64_t n, int64_t k, int sm_count);
 
 int read_and_clear_error_word(bool clear);
+// Runs a kernel whose bounded mbarrier wait can never be satisfied; returns
+// the error code it recorded (expected non-zero), or -1 on a CUDA error.
+int selftest_bounded_wait(uint32_t timeout_us);
 uint64_t launch_count();
 
 }  // namespace zcb
