@@ -344,18 +344,27 @@ def run_gpu(args) -> int:
 
 
 def run_e2e(args, layer, x_host, device, barrier, max_over_ranks, total_flops) -> dict:
-    """Same step with host buffers: H2D of the layer input (pinned) on one copy
-    stream, D2H of the layer output on another, both double-buffered so the
-    copies of step i+1 / i-1 overlap the GEMMs of step i. All inside the timed region."""
+    """Same step with host buffers, whole job copying the input once and the
+    output once: rank r copies rows [r0, r1) of the layer input from pinned
+    host memory (H2D stream), an NCCL all-gather over NVLink assembles the
+    full input on every rank, and rank r copies rows [r0, r1) of the
+    all-reduced output back (D2H stream). Buffers are double-buffered so the
+    copies of step i+1 / i-1 overlap the GEMMs of step i; all inside the timed region."""
     import torch
+    import torch.distributed as dist
 
+    from zcutlass_b200.tp import shard_range
+
+    world, rank = layer.tp.world_size, layer.tp.rank
     compute = torch.cuda.current_stream(device)
     h2d_s, d2h_s = torch.cuda.Stream(device), torch.cuda.Stream(device)
-    hx = x_host.pin_memory()
-    dx = [torch.empty_like(hx, device=device) for _ in range(2)]
-    hidden = layer.shape.hidden
-    dout = [torch.empty(hx.shape[0], hidden, device=device, dtype=hx.dtype) for _ in range(2)]
-    hout = [torch.empty(hx.shape[0], hidden, dtype=hx.dtype).pin_memory() for _ in range(2)]
+    m, hidden = x_host.shape
+    r0, r1 = shard_range(m, rank, world)
+    hx = x_host[r0:r1].contiguous().pin_memory()
+    dx_part = [torch.empty_like(hx, device=device) for _ in range(2)]
+    dx = dx_part if world == 1 else [torch.empty(m, hidden, device=device, dtype=hx.dtype) for _ in range(2)]
+    dout = [torch.empty(m, layer.shape.hidden, device=device, dtype=hx.dtype) for _ in range(2)]
+    hout = [torch.empty(r1 - r0, layer.shape.hidden, dtype=hx.dtype).pin_memory() for _ in range(2)]
     e = lambda: torch.cuda.Event()  # noqa: E731
     h2d_ev, d2h_ev, comp_ev = [e(), e()], [e(), e()], [e(), e()]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -365,24 +374,26 @@ def run_e2e(args, layer, x_host, device, barrier, max_over_ranks, total_flops) -
         start.record(compute)
         h2d_s.wait_event(start)
         with torch.cuda.stream(h2d_s):
-            dx[0].copy_(hx, non_blocking=True)
+            dx_part[0].copy_(hx, non_blocking=True)
         h2d_ev[0].record(h2d_s)
         for i in range(n):
             s = i % 2
             compute.wait_event(h2d_ev[s])
             if i >= 2:
                 compute.wait_event(d2h_ev[s])
+            if world > 1:
+                dist.all_gather_into_tensor(dx[s], dx_part[s], group=layer.tp.group)
             layer.forward(dx[s], out=dout[s])
             comp_ev[s].record(compute)
             if i + 1 < n:
                 if i >= 1:
                     h2d_s.wait_event(comp_ev[1 - s])
                 with torch.cuda.stream(h2d_s):
-                    dx[1 - s].copy_(hx, non_blocking=True)
+                    dx_part[1 - s].copy_(hx, non_blocking=True)
                 h2d_ev[1 - s].record(h2d_s)
             d2h_s.wait_event(comp_ev[s])
             with torch.cuda.stream(d2h_s):
-                hout[s].copy_(dout[s], non_blocking=True)
+                hout[s].copy_(dout[s][r0:r1], non_blocking=True)
             d2h_ev[s].record(d2h_s)
         compute.wait_event(d2h_ev[(n - 1) % 2])
         end.record(compute)
@@ -393,9 +404,10 @@ def run_e2e(args, layer, x_host, device, barrier, max_over_ranks, total_flops) -
     loop(steps)
     ms = max_over_ranks(start.elapsed_time(end)) / steps
     barrier()
-    nbytes = hx.numel() * hx.element_size()
     return {"value": round(total_flops / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
-            "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": dout[0].numel() * dout[0].element_size(),
+            "h2d_bytes_per_step": m * hidden * hx.element_size(),
+            "d2h_bytes_per_step": m * layer.shape.hidden * hx.element_size(),
+            "copies": "whole job: input rows split over ranks (H2D) + NCCL all-gather; output rows split (D2H)",
             "api": "C ABI zcutlass_gemm (include/zcutlass_c.h) via zcutlass_b200.tp"}
 
 

@@ -103,7 +103,7 @@ def sel(m, n, k, dtype=N.BF16, **kw):
 
 
 def test_registered_operation_count():
-    assert N.lib().zcutlass_registered_gemm_operation_count() == 14
+    assert N.lib().zcutlass_registered_gemm_operation_count() == 20
 
 
 def test_shape_families_follow_reference_rules():
@@ -151,6 +151,18 @@ def test_experimental_flags_do_not_change_default_dispatch(monkeypatch):
     monkeypatch.setenv("ZCUTLASS_EXPERIMENTAL_KERNELS", "1")
     monkeypatch.setenv("ZCUTLASS_EXPERIMENTAL_KERNEL", "anything")
     assert sel(128, 4096, 4096)["kernel_name"] == base
+
+
+def test_experimental_streamk_decode(monkeypatch):
+    # the stream-K decode family is experimental (reference semantics: gated by
+    # ZCUTLASS_EXPERIMENTAL_KERNELS and the ZCUTLASS_EXPERIMENTAL_KERNEL filter)
+    d = sel(16, 7168, 8192)
+    assert "swapab_splitk" in d["kernel_name"] and d["kernel_path"] == "fast"
+    monkeypatch.setenv("ZCUTLASS_EXPERIMENTAL_KERNELS", "1")
+    e = sel(16, 7168, 8192)
+    assert "swapab_streamk" in e["kernel_name"] and e["kernel_path"] == "experimental_fast"
+    monkeypatch.setenv("ZCUTLASS_EXPERIMENTAL_KERNEL", "no_match")
+    assert "swapab_splitk" in sel(16, 7168, 8192)["kernel_name"]
 
 
 def test_gemm_desc_layout_matches_c_header():

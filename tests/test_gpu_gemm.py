@@ -61,9 +61,12 @@ FAMILIES = {
     "pair256": "_256x256x64_2cta_persistent",
     "persistent256": "_128x256x64_ws_persistent",
     "persistent128": "_128x128x64_ws_persistent",
-    "swapab16": "_16x128x64_swapab",
-    "swapab32": "_32x128x64_swapab",
-    "swapab64": "_64x128x64_swapab",
+    "swapab16": "_16x128x64_swapab_splitk",
+    "swapab32": "_32x128x64_swapab_splitk",
+    "swapab64": "_64x128x64_swapab_splitk",
+    "sk16": "_16x128x64_swapab_streamk",
+    "sk32": "_32x128x64_swapab_streamk",
+    "sk64": "_64x128x64_swapab_streamk",
     "generic": "_generic",
 }
 
@@ -76,6 +79,11 @@ FAMILY_SHAPES = {
     "swapab16": [(1, 128, 128), (7, 300, 200), (16, 1000, 4096), (13, 4096, 1032)],
     "swapab32": [(17, 128, 128), (32, 520, 777), (25, 2048, 2048)],
     "swapab64": [(33, 256, 256), (64, 1000, 1000), (48, 4096, 1536)],
+    # stream-K: one tile split over 128 CTAs, a 12-unit problem (every tile
+    # shared by several CTAs), ragged edges, and decode-sized layers
+    "sk16": [(1, 128, 8192), (7, 300, 200), (16, 1000, 4096), (13, 7168, 1032), (16, 8192, 1024)],
+    "sk32": [(17, 128, 128), (32, 520, 777), (25, 2048, 8192)],
+    "sk64": [(33, 256, 256), (64, 1000, 1000), (48, 4096, 1536)],
     "generic": [(5, 7, 9), (100, 200, 50), (130, 70, 300)],
 }
 
@@ -155,3 +163,67 @@ def test_config_shapes_sampled(cuda_device, case, col):
     ref = oracle.gemm_f64_rows(a, b_rm, rows, n, k, dt, c=cm, bias=bvec if bias else None, alpha=1.0, beta=beta)
     out = oracle.bits_to_float(d[rows, :n], dt)
     oracle.check(out, ref, dt)
+
+
+# ---------------------------------------------------------------- stream-K specifics
+
+
+def _sk_run(m, n, k, dtype, stream=None, repeats=1):
+    import torch
+
+    g = torch.Generator(device="cpu").manual_seed(3)
+    tdt = torch.bfloat16 if dtype == BF16 else torch.float16
+    a = torch.randn(m, k, generator=g).to(tdt).cuda()
+    w = (torch.randn(n, k, generator=g) / k ** 0.5).to(tdt).cuda()
+    outs = []
+    for _ in range(repeats):
+        d = torch.empty(m, n, dtype=tdt, device="cuda")
+        desc = _native.make_desc(m, n, k, k, k, n, n, dtype, stream=stream, b_layout=_native.COLUMN_MAJOR)
+        assert _native.gemm(desc, a.data_ptr(), w.data_ptr(), None, d.data_ptr()) == 0
+        outs.append(d)
+    return a, w, outs
+
+
+@pytest.mark.gpu
+def test_streamk_is_deterministic(cuda_device, monkeypatch):
+    import torch
+
+    monkeypatch.setenv("ZCUTLASS_FORCE_KERNEL", "_16x128x64_swapab_streamk")
+    _, _, outs = _sk_run(16, 7168, 8192, BF16, repeats=4)
+    torch.cuda.synchronize()
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    assert _native.device_error(clear=True) == 0
+
+
+@pytest.mark.gpu
+def test_streamk_in_cuda_graph_replays(cuda_device, monkeypatch):
+    """The counters reset themselves, so a captured launch (fixed epoch)
+    replays correctly; interleaved shapes on one stream share the workspace."""
+    import torch
+
+    monkeypatch.setenv("ZCUTLASS_FORCE_KERNEL", "_swapab_streamk")
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        a, w, (ref,) = _sk_run(8, 1280, 8192, BF16, stream=s.cuda_stream)  # allocates the workspace
+        a2, w2, (ref2,) = _sk_run(32, 4096, 1024, BF16, stream=s.cuda_stream)
+        torch.cuda.synchronize()
+        d = torch.empty_like(ref)
+        d2 = torch.empty_like(ref2)
+        desc = _native.make_desc(8, 1280, 8192, 8192, 8192, 1280, 1280, BF16, stream=s.cuda_stream,
+                                 b_layout=_native.COLUMN_MAJOR)
+        desc2 = _native.make_desc(32, 4096, 1024, 1024, 1024, 4096, 4096, BF16, stream=s.cuda_stream,
+                                  b_layout=_native.COLUMN_MAJOR)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            desc.stream = torch.cuda.current_stream().cuda_stream
+            desc2.stream = desc.stream
+            assert _native.gemm(desc, a.data_ptr(), w.data_ptr(), None, d.data_ptr()) == 0
+            assert _native.gemm(desc2, a2.data_ptr(), w2.data_ptr(), None, d2.data_ptr()) == 0
+        for _ in range(3):
+            d.zero_()
+            d2.zero_()
+            g.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(d, ref) and torch.equal(d2, ref2)
+    assert _native.device_error(clear=True) == 0

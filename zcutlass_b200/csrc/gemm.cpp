@@ -127,7 +127,7 @@ SelectDevice select_device() {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-enum class Kind { UmmaPair, UmmaPersistent, UmmaSwapAb, Generic };
+enum class Kind { UmmaPair, UmmaPersistent, UmmaSwapAb, UmmaSwapAbStreamK, Generic };
 
 class Sm100Operation final : public GemmOperation {
  public:
@@ -146,7 +146,10 @@ class Sm100Operation final : public GemmOperation {
     desc_.requires_aligned_tiles = kind != Kind::Generic;
     desc_.supports_beta = true;
     desc_.supports_bias = true;
-    desc_.experimental = false;
+    // Stream-K decode: correct and deterministic, but its partial-tile fixup
+    // makes it slower than cluster split-K on every measured decode shape, so
+    // it runs only when experimental kernels are enabled (or it is forced).
+    desc_.experimental = kind == Kind::UmmaSwapAbStreamK;
     desc_.pipeline_stages = stages;
     desc_.epilogue = epilogue;
   }
@@ -159,8 +162,8 @@ class Sm100Operation final : public GemmOperation {
     if (args.A.layout != layout::LayoutKind::RowMajor || args.C.layout != layout::LayoutKind::RowMajor ||
         args.D.layout != layout::LayoutKind::RowMajor)
       return false;
-    if (desc_.experimental && !experimental_allowed(desc_.name)) return false;
     if (!force_filter_allows(desc_.name)) return false;
+    if (desc_.experimental && !force_filter_active() && !experimental_allowed(desc_.name)) return false;
     const int64_t m = args.problem.m, n = args.problem.n, k = args.problem.k;
     if (kind_ == Kind::Generic) return true;
 
@@ -172,12 +175,15 @@ class Sm100Operation final : public GemmOperation {
       return false;
 
     const bool forced = force_filter_active();
-    if (kind_ == Kind::UmmaSwapAb) {
+    if (kind_ == Kind::UmmaSwapAb || kind_ == Kind::UmmaSwapAbStreamK) {
       const int mp = desc_.tile_m;
       if (m > mp) return false;
       if (forced) return true;
       if (mp > 16 && m <= mp / 2) return false;
-      return n >= 128 && k >= 128;
+      if (n < 128 || k < 128) return false;
+      // Split-K takes every bucketed shape; an enabled stream-K operation
+      // (listed first) takes the shapes where split-K would idle SMs.
+      return kind_ == Kind::UmmaSwapAb || zcb::swapab_prefer_streamk(n, k, dev.sm_count);
     }
     // Persistent kernel: D goes out through TMA; C and bias are read with
     // 16-byte vector loads.
@@ -217,6 +223,9 @@ class Sm100Operation final : public GemmOperation {
       case Kind::UmmaPersistent:
         e = zcb::launch_umma_gemm(la, desc_.tile_n);
         break;
+      case Kind::UmmaSwapAbStreamK:
+        e = zcb::launch_umma_swapab_sk_gemm(la);
+        break;
       case Kind::UmmaSwapAb:
         e = zcb::launch_umma_swapab_gemm(la, nullptr);
         break;
@@ -244,6 +253,12 @@ void register_builtin_operations() {
   // wave-quantisation model in choose_persistent picks), then the predicated
   // CUDA-core kernel that accepts any layout.
   static const Sm100Operation ops[] = {
+      {"zcutlass_sm100_tcgen05_bf16_16x128x64_swapab_streamk", DType::BF16, K::UmmaSwapAbStreamK, 16, 128, 64, 12, F::Decode, E::RegisterLinear},
+      {"zcutlass_sm100_tcgen05_f16_16x128x64_swapab_streamk", DType::F16, K::UmmaSwapAbStreamK, 16, 128, 64, 12, F::Decode, E::RegisterLinear},
+      {"zcutlass_sm100_tcgen05_bf16_32x128x64_swapab_streamk", DType::BF16, K::UmmaSwapAbStreamK, 32, 128, 64, 11, F::Decode, E::RegisterLinear},
+      {"zcutlass_sm100_tcgen05_f16_32x128x64_swapab_streamk", DType::F16, K::UmmaSwapAbStreamK, 32, 128, 64, 11, F::Decode, E::RegisterLinear},
+      {"zcutlass_sm100_tcgen05_bf16_64x128x64_swapab_streamk", DType::BF16, K::UmmaSwapAbStreamK, 64, 128, 64, 9, F::Prefill, E::RegisterLinear},
+      {"zcutlass_sm100_tcgen05_f16_64x128x64_swapab_streamk", DType::F16, K::UmmaSwapAbStreamK, 64, 128, 64, 9, F::Prefill, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_bf16_16x128x64_swapab_splitk", DType::BF16, K::UmmaSwapAb, 16, 128, 64, 10, F::Decode, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_f16_16x128x64_swapab_splitk", DType::F16, K::UmmaSwapAb, 16, 128, 64, 10, F::Decode, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_bf16_32x128x64_swapab_splitk", DType::BF16, K::UmmaSwapAb, 32, 128, 64, 9, F::Decode, E::RegisterLinear},

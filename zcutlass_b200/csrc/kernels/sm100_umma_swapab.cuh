@@ -36,14 +36,19 @@ struct SwapAbParams {
 namespace swapab {
 
 constexpr int kBlockN = 128;  // rows of D^T per CTA (MMA M)
-constexpr int kBlockK = 64;
+constexpr int kBlockK = 64;   // one 128-byte swizzle row of K; a stage holds KSUB of them
 constexpr int kThreads = 192;
 
-template <int MP, int STAGES>
+// A pipeline stage holds KSUB K sub-blocks of 64: TMA streams a weight
+// matrix at ~4.7 TB/s with 16 KiB per stage but ~5.7 TB/s with >= 32 KiB
+// (measured on B200, independent of ring depth), so decode uses KSUB = 2.
+template <int MP, int STAGES, int KSUB = 1>
 struct Smem {
   static constexpr int kWChunkBytes = kBlockK * 128;       // 64(n) x 64(k) box: 8 KiB
-  static constexpr int kWBytes = 2 * kWChunkBytes;          // 128(n) x 64(k): 16 KiB
-  static constexpr int kXBytes = MP * 128;                  // MP(m) x 64(k)
+  static constexpr int kWSubBytes = 2 * kWChunkBytes;       // 128(n) x 64(k): 16 KiB
+  static constexpr int kXSubBytes = MP * 128;               // MP(m) x 64(k)
+  static constexpr int kWBytes = KSUB * kWSubBytes;
+  static constexpr int kXBytes = KSUB * kXSubBytes;
   static constexpr int kStageBytes = kWBytes + kXBytes;
   static constexpr int kWOff = 0;
   static constexpr int kXOff = STAGES * kWBytes;
@@ -81,11 +86,12 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
 
 // kWKMajor: the weight matrix is column-major B (a PyTorch [N, K] weight), so
 // its 128(n) x 64(k) tile is one K-major box instead of two N-major boxes.
-template <typename T, int MP, int STAGES, bool kWKMajor>
+// p.num_kb counts K blocks of KSUB * 64.
+template <typename T, int MP, int STAGES, int KSUB, bool kWKMajor>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                 const SwapAbParams p) {
-  using L = Smem<MP, STAGES>;
+  using L = Smem<MP, STAGES, KSUB>;
   constexpr uint32_t kTmemCols = MP < 32 ? 32 : MP;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -142,15 +148,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         mbar_arrive_expect_tx(&full[s], L::kStageBytes);
-        uint8_t* w = smem + L::kWOff + s * L::kWBytes;
-        if constexpr (kWKMajor) {
-          tma_load_2d_hint(w, &tmap_w, &full[s], kb * kBlockK, n0, stream_once);
-        } else {
-          tma_load_2d_hint(w, &tmap_w, &full[s], n0, kb * kBlockK, stream_once);
-          tma_load_2d_hint(w + L::kWChunkBytes, &tmap_w, &full[s], n0 + 64, kb * kBlockK,
-                           stream_once);
+#pragma unroll
+        for (int sub = 0; sub < KSUB; ++sub) {
+          const int k0 = (kb * KSUB + sub) * kBlockK;
+          uint8_t* w = smem + L::kWOff + s * L::kWBytes + sub * L::kWSubBytes;
+          if constexpr (kWKMajor) {
+            tma_load_2d_hint(w, &tmap_w, &full[s], k0, n0, stream_once);
+          } else {
+            tma_load_2d_hint(w, &tmap_w, &full[s], n0, k0, stream_once);
+            tma_load_2d_hint(w + L::kWChunkBytes, &tmap_w, &full[s], n0 + 64, k0, stream_once);
+          }
+          tma_load_2d_hint(smem + L::kXOff + s * L::kXBytes + sub * L::kXSubBytes, &tmap_x, &full[s], k0, 0,
+                           keep);
         }
-        tma_load_2d_hint(smem + L::kXOff + s * L::kXBytes, &tmap_x, &full[s], kb * kBlockK, 0, keep);
       }
       if (!ok) {
         const uint32_t first = it > static_cast<uint32_t>(STAGES) ? it - STAGES : 0u;
@@ -173,15 +183,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after_sync();
-        const uint32_t w_addr = smem_addr(smem + L::kWOff + s * L::kWBytes);
-        const uint32_t x_addr = smem_addr(smem + L::kXOff + s * L::kXBytes);
 #pragma unroll
-        for (int kk = 0; kk < kBlockK / 16; ++kk) {
-          const uint64_t a_desc = kWKMajor
-                                      ? smem_desc_sw128(w_addr + kk * 32, 16, 1024)
-                                      : smem_desc_sw128(w_addr + kk * 2048, L::kWChunkBytes, 1024);
-          const uint64_t b_desc = smem_desc_sw128(x_addr + kk * 32, 16, 1024);
-          umma_f16_ss(tmem_base, a_desc, b_desc, kIdesc, (it | kk) != 0 ? 1u : 0u);
+        for (int sub = 0; sub < KSUB; ++sub) {
+          const uint32_t w_addr = smem_addr(smem + L::kWOff + s * L::kWBytes + sub * L::kWSubBytes);
+          const uint32_t x_addr = smem_addr(smem + L::kXOff + s * L::kXBytes + sub * L::kXSubBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBlockK / 16; ++kk) {
+            const uint64_t a_desc = kWKMajor ? smem_desc_sw128(w_addr + kk * 32, 16, 1024)
+                                             : smem_desc_sw128(w_addr + kk * 2048, L::kWChunkBytes, 1024);
+            const uint64_t b_desc = smem_desc_sw128(x_addr + kk * 32, 16, 1024);
+            umma_f16_ss(tmem_base, a_desc, b_desc, kIdesc, (it | sub | kk) != 0 ? 1u : 0u);
+          }
         }
         issued = true;
         umma_commit(&empty[s]);

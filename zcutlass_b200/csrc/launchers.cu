@@ -9,7 +9,11 @@
 #include "kernels/sm100_umma_gemm.cuh"
 #include "kernels/sm100_umma_gemm_2cta.cuh"
 #include "kernels/sm100_umma_swapab.cuh"
+#include "kernels/sm100_umma_swapab_sk.cuh"
 #include "tma_desc.hpp"
+
+#include <map>
+#include <utility>
 
 namespace zcb {
 
@@ -21,6 +25,11 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 std::atomic<uint64_t> g_launches{0};
+
+// Decode (swap-AB) kernels stage 2 x 64 of K per pipeline slot: 32 KiB of
+// weights per stage, which TMA streams at ~5.7 TB/s (16 KiB stages: ~4.7).
+constexpr int kDecodeKsub = 2;
+constexpr int kDecodeKBlock = 64 * kDecodeKsub;
 
 struct DeviceSlot {
   std::once_flag once;
@@ -104,7 +113,7 @@ cudaError_t launch_umma_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit)
 
 template <typename T, int MP, int STAGES, bool KM>
 cudaError_t launch_swapab_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit, int splits) {
-  using L = swapab::Smem<MP, STAGES>;
+  using L = swapab::Smem<MP, STAGES, kDecodeKsub>;
   CUtensorMap tw, tx;
   const bool bf16 = a.bf16;
   // Weights: the B matrix ([K, N] row-major, or [N, K] when column-major);
@@ -120,7 +129,7 @@ cudaError_t launch_swapab_t(const LaunchArgs& a, DeviceSlot* slot, int config_bi
   p.m = static_cast<int>(a.m);
   p.n = static_cast<int>(a.n);
   p.k = static_cast<int>(a.k);
-  p.num_kb = static_cast<int>((a.k + swapab::kBlockK - 1) / swapab::kBlockK);
+  p.num_kb = static_cast<int>((a.k + kDecodeKBlock - 1) / kDecodeKBlock);
   p.splits = splits;
   p.alpha = a.alpha;
   p.beta = a.beta;
@@ -132,7 +141,7 @@ cudaError_t launch_swapab_t(const LaunchArgs& a, DeviceSlot* slot, int config_bi
   p.epi_flags = (a.beta != 0.0f ? kEpiHasC : 0u) | (a.bias != nullptr ? kEpiHasBias : 0u);
   p.error_word = slot->info.error_word;
 
-  auto kernel = swapab::gemm_kernel<T, MP, STAGES, KM>;
+  auto kernel = swapab::gemm_kernel<T, MP, STAGES, kDecodeKsub, KM>;
   cudaError_t e = ensure_smem_attr(slot, config_bit, kernel, L::kDynamicBytes);
   if (e != cudaSuccess) return e;
 
@@ -219,6 +228,88 @@ cudaError_t launch_umma2_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit
   return cudaGetLastError();
 }
 
+// Stream-K workspace, one per (device, stream): tile counters followed by the
+// FP32 partial slots. Kernels on one stream run in order, so they can share
+// it; kernels on different streams may overlap, so they never do. Grown on
+// demand (after draining the stream that used the old buffer); the counter
+// region is zeroed when allocated and epoch-tagged afterwards.
+struct StreamKWorkspace {
+  void* base = nullptr;
+  size_t counter_bytes = 0;  // fixed-size counter region at the front
+  size_t partial_bytes = 0;  // partial slots after it
+  uint32_t epoch = 0;
+};
+std::mutex g_ws_mutex;
+std::map<std::pair<int, cudaStream_t>, StreamKWorkspace> g_ws;
+
+cudaError_t acquire_workspace(int dev, cudaStream_t stream, size_t counter_need, size_t partial_need,
+                              unsigned long long** counters, float** partials, uint32_t* epoch) {
+  std::lock_guard<std::mutex> lock(g_ws_mutex);
+  StreamKWorkspace& ws = g_ws[{dev, stream}];
+  if (ws.counter_bytes < counter_need || ws.partial_bytes < partial_need) {
+    if (ws.base != nullptr) {
+      cudaError_t e = cudaStreamSynchronize(stream);  // the old buffer may still be in use
+      if (e != cudaSuccess) return e;
+      cudaFree(ws.base);
+      ws = StreamKWorkspace{nullptr, 0, 0, ws.epoch};
+    }
+    const size_t ctr = std::max<size_t>((counter_need + 255) & ~size_t(255), size_t(64) << 10);
+    const size_t part = std::max<size_t>((partial_need + 255) & ~size_t(255), size_t(4) << 20);
+    cudaError_t e = cudaMalloc(&ws.base, ctr + part);
+    if (e != cudaSuccess) return e;
+    e = cudaMemsetAsync(ws.base, 0, ctr, stream);  // counters start at (epoch 0, count 0)
+    if (e != cudaSuccess) return e;
+    ws.counter_bytes = ctr;
+    ws.partial_bytes = part;
+  }
+  ws.epoch = ws.epoch + 1 == 0 ? 1 : ws.epoch + 1;  // never 0: zeroed counters read as stale
+  *counters = static_cast<unsigned long long*>(ws.base);
+  *partials = reinterpret_cast<float*>(static_cast<char*>(ws.base) + ws.counter_bytes);
+  *epoch = ws.epoch;
+  return cudaSuccess;
+}
+
+template <typename T, int MP, int STAGES, bool KM>
+cudaError_t launch_swapab_sk_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit) {
+  using L = swapab_sk::Smem<MP, STAGES, kDecodeKsub>;
+  CUtensorMap tw, tx;
+  const bool bf16 = a.bf16;
+  const bool w_ok =
+      KM ? make_tma_2d(&tw, a.b, bf16, a.n, a.k, a.ldb, swapab_sk::kBlockN, swapab_sk::kBlockK, TmaSwizzle::B128)
+         : make_tma_2d(&tw, a.b, bf16, a.k, a.n, a.ldb, swapab_sk::kBlockK, 64, TmaSwizzle::B128);
+  if (!w_ok || !make_tma_2d(&tx, a.a, bf16, a.m, a.k, a.lda, MP, swapab_sk::kBlockK, TmaSwizzle::B128)) {
+    return cudaErrorInvalidValue;
+  }
+  SwapAbSkParams p{};
+  p.m = static_cast<int>(a.m);
+  p.n = static_cast<int>(a.n);
+  p.k = static_cast<int>(a.k);
+  p.num_kb = static_cast<int>((a.k + kDecodeKBlock - 1) / kDecodeKBlock);
+  p.tiles_n = static_cast<int>((a.n + swapab_sk::kBlockN - 1) / swapab_sk::kBlockN);
+  p.total_units = static_cast<long long>(p.num_kb) * p.tiles_n;
+  p.grid = static_cast<int>(std::min<long long>(p.total_units, slot->info.sm_count));
+  p.alpha = a.alpha;
+  p.beta = a.beta;
+  p.c = a.c;
+  p.ldc = a.ldc;
+  p.d = a.d;
+  p.ldd = a.ldd;
+  p.bias = a.bias;
+  p.epi_flags = (a.beta != 0.0f ? kEpiHasC : 0u) | (a.bias != nullptr ? kEpiHasBias : 0u);
+  p.error_word = slot->info.error_word;
+  cudaError_t e = acquire_workspace(slot->info.ordinal, a.stream, size_t(p.tiles_n) * 8,
+                                    size_t(2) * p.grid * MP * swapab_sk::kBlockN * sizeof(float), &p.counters,
+                                    &p.partials, &p.epoch);
+  if (e != cudaSuccess) return e;
+
+  auto kernel = swapab_sk::gemm_kernel<T, MP, STAGES, kDecodeKsub, KM>;
+  e = ensure_smem_attr(slot, config_bit, kernel, L::kDynamicBytes);
+  if (e != cudaSuccess) return e;
+  kernel<<<p.grid, swapab_sk::kThreads, L::kDynamicBytes, a.stream>>>(tw, tx, p);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return cudaGetLastError();
+}
+
 template <typename T>
 cudaError_t launch_generic_t(const LaunchArgs& a) {
   GenericGemmParams p{a.m,   a.n,   a.k,   a.a,     a.lda,  a.b,   a.ldb,
@@ -248,8 +339,29 @@ enum : int {
   kCfgSwapF16M64,
   kCfgPairBf16,
   kCfgPairF16,
-  kCfgColMajorB = 16,
+  kCfgSkBf16M16,
+  kCfgSkF16M16,
+  kCfgSkBf16M32,
+  kCfgSkF16M32,
+  kCfgSkBf16M64,
+  kCfgSkF16M64,
+  kCfgColMajorB = 32,
 };
+
+template <bool KM>
+cudaError_t launch_swapab_sk_km(const LaunchArgs& a, DeviceSlot* slot) {
+  const int off = KM ? kCfgColMajorB : 0;
+  if (a.m <= 16) {
+    return a.bf16 ? launch_swapab_sk_t<__nv_bfloat16, 16, 6, KM>(a, slot, kCfgSkBf16M16 + off)
+                  : launch_swapab_sk_t<half, 16, 6, KM>(a, slot, kCfgSkF16M16 + off);
+  }
+  if (a.m <= 32) {
+    return a.bf16 ? launch_swapab_sk_t<__nv_bfloat16, 32, 5, KM>(a, slot, kCfgSkBf16M32 + off)
+                  : launch_swapab_sk_t<half, 32, 5, KM>(a, slot, kCfgSkF16M32 + off);
+  }
+  return a.bf16 ? launch_swapab_sk_t<__nv_bfloat16, 64, 4, KM>(a, slot, kCfgSkBf16M64 + off)
+                : launch_swapab_sk_t<half, 64, 4, KM>(a, slot, kCfgSkF16M64 + off);
+}
 
 template <bool KM>
 cudaError_t launch_umma_km(const LaunchArgs& a, DeviceSlot* slot, int bn) {
@@ -266,15 +378,15 @@ template <bool KM>
 cudaError_t launch_swapab_km(const LaunchArgs& a, DeviceSlot* slot, int splits) {
   const int off = KM ? kCfgColMajorB : 0;
   if (a.m <= 16) {
-    return a.bf16 ? launch_swapab_t<__nv_bfloat16, 16, 10, KM>(a, slot, kCfgSwapBf16M16 + off, splits)
-                  : launch_swapab_t<half, 16, 10, KM>(a, slot, kCfgSwapF16M16 + off, splits);
+    return a.bf16 ? launch_swapab_t<__nv_bfloat16, 16, 5, KM>(a, slot, kCfgSwapBf16M16 + off, splits)
+                  : launch_swapab_t<half, 16, 5, KM>(a, slot, kCfgSwapF16M16 + off, splits);
   }
   if (a.m <= 32) {
-    return a.bf16 ? launch_swapab_t<__nv_bfloat16, 32, 9, KM>(a, slot, kCfgSwapBf16M32 + off, splits)
-                  : launch_swapab_t<half, 32, 9, KM>(a, slot, kCfgSwapF16M32 + off, splits);
+    return a.bf16 ? launch_swapab_t<__nv_bfloat16, 32, 5, KM>(a, slot, kCfgSwapBf16M32 + off, splits)
+                  : launch_swapab_t<half, 32, 5, KM>(a, slot, kCfgSwapF16M32 + off, splits);
   }
-  return a.bf16 ? launch_swapab_t<__nv_bfloat16, 64, 7, KM>(a, slot, kCfgSwapBf16M64 + off, splits)
-                : launch_swapab_t<half, 64, 7, KM>(a, slot, kCfgSwapF16M64 + off, splits);
+  return a.bf16 ? launch_swapab_t<__nv_bfloat16, 64, 4, KM>(a, slot, kCfgSwapBf16M64 + off, splits)
+                : launch_swapab_t<half, 64, 4, KM>(a, slot, kCfgSwapF16M64 + off, splits);
 }
 
 }  // namespace
@@ -316,7 +428,7 @@ PersistentConfig choose_persistent(int64_t m, int64_t n, int sm_count) {
 
 int swapab_choose_splits(int64_t n, int64_t k, int sm_count) {
   const int64_t tiles_n = (n + swapab::kBlockN - 1) / swapab::kBlockN;
-  const int64_t num_kb = (k + swapab::kBlockK - 1) / swapab::kBlockK;
+  const int64_t num_kb = (k + kDecodeKBlock - 1) / kDecodeKBlock;
   int64_t s = sm_count / std::max<int64_t>(tiles_n, 1);
   s = std::min<int64_t>(s, 8);
   s = std::min<int64_t>(s, num_kb);
@@ -339,6 +451,20 @@ cudaError_t launch_umma_pair_gemm(const LaunchArgs& a) {
   }
   return a.bf16 ? launch_umma2_t<__nv_bfloat16, 6, false>(a, slot, kCfgPairBf16 + off)
                 : launch_umma2_t<half, 6, false>(a, slot, kCfgPairF16 + off);
+}
+
+cudaError_t launch_umma_swapab_sk_gemm(const LaunchArgs& a) {
+  DeviceSlot* slot = current_slot();
+  if (slot == nullptr) return cudaErrorInvalidDevice;
+  return a.b_col_major ? launch_swapab_sk_km<true>(a, slot) : launch_swapab_sk_km<false>(a, slot);
+}
+
+bool swapab_prefer_streamk(int64_t n, int64_t k, int sm_count) {
+  // Cluster split-K fills tiles_n x splits SMs; stream-K always fills all of
+  // them. Prefer stream-K unless split-K already covers ~95% of the SMs.
+  const int64_t tiles_n = (n + swapab::kBlockN - 1) / swapab::kBlockN;
+  const int64_t used = tiles_n * swapab_choose_splits(n, k, sm_count);
+  return used * 100 < static_cast<int64_t>(sm_count) * 95;
 }
 
 cudaError_t launch_umma_swapab_gemm(const LaunchArgs& a, int* splits_used) {

@@ -42,6 +42,11 @@ cudaError_t launch_umma_pair_gemm(const LaunchArgs& args);
 // Swap-AB tcgen05 kernel for small M (M <= 32): split-K across a thread-block
 // cluster, reduced through distributed shared memory.
 cudaError_t launch_umma_swapab_gemm(const LaunchArgs& args, int* splits_used);
+// Stream-K swap-AB kernel for small M (M <= 64): every SM streams an equal
+// share of the weights; partial tiles are reduced through a per-stream
+// workspace owned by the library.
+cudaError_t launch_umma_swapab_sk_gemm(const LaunchArgs& args);
+bool swapab_prefer_streamk(int64_t n, int64_t k, int sm_count);
 // Predicated CUDA-core kernel for TMA-incompatible layouts.
 cudaError_t launch_generic_gemm(const LaunchArgs& args);
 
