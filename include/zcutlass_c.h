@@ -109,6 +109,36 @@ int zcutlass_device_error(int clear);
 /* Number of kernel launches this library has enqueued since load (all devices). */
 uint64_t zcutlass_gemm_kernel_launches(void);
 
+/* Decode GEMM that allocates nothing (no counterpart in the reference).
+ *
+ * For callers that cannot call cudaMalloc: code running while a CUDA graph is
+ * being captured or inside a custom allocator/memory-pool callback, or hosts
+ * that forbid device allocation after start-up. The regular entry points may
+ * allocate a per-stream workspace the first time the stream-K decode kernel
+ * runs on a stream; this one runs that kernel with its scratch in a fixed
+ * 16 MiB array compiled into the library (every GPU that loads the library
+ * holds it until the process exits) and calls no cudaMalloc, cudaFree or
+ * allocating library routine.
+ *
+ *   D[M,N] = alpha * A[M,K] * B + beta * C + bias[N]   (f16/bf16, FP32 accumulate)
+ *   B is [K,N] row-major (b_col_major = 0) or a [N,K] weight (b_col_major = 1).
+ *
+ * Limits: 1 <= M <= 64; A and B 16-byte aligned with lda, ldb multiples of 8;
+ * scratch needed = 64 KiB of tile counters (N <= 1,048,576) + 2 * G * MP * 512
+ * bytes of partials (G = min(#SMs, ceil(N/128) * ceil(K/128)), MP = 16, 32 or
+ * 64 by M) must fit in 16 MiB. Anything outside these limits returns
+ * ZCUTLASS_INVALID_ARGUMENT without launching; other argument errors return
+ * the same codes as zcutlass_gemm.
+ * The first call on each device looks up the scratch array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls share the one array and each call clears the counters it uses
+ * on `stream` before its kernel: calls whose kernels overlap on the GPU (on
+ * different streams) race, so serialise them. */
+int zcutlass_gemm_decode_noalloc(int64_t m, int64_t n, int64_t k, const void* A, int64_t lda,
+                                 const void* B, int64_t ldb, int32_t b_col_major, const void* C,
+                                 int64_t ldc, void* D, int64_t ldd, int32_t dtype, float alpha,
+                                 float beta, const void* bias, void* stream);
+
 /* Failure-detection self test (no reference counterpart): launches one kernel
  * whose bounded mbarrier wait is never satisfied, with a limit of `timeout_us`
  * microseconds. The wait gives up, records an error code and the kernel

@@ -117,4 +117,48 @@ uint64_t zcutlass_gemm_kernel_launches(void) { return zcb::launch_count(); }
 
 int zcutlass_selftest_bounded_wait(uint32_t timeout_us) { return zcb::selftest_bounded_wait(timeout_us); }
 
+// For callers that may not allocate device memory at call time (see the
+// header): same validation as zcutlass_gemm, then the stream-K decode kernel
+// with its scratch in the library's fixed device array.
+int zcutlass_gemm_decode_noalloc(int64_t m, int64_t n, int64_t k, const void* A, int64_t lda,
+                                 const void* B, int64_t ldb, int32_t b_col_major, const void* C,
+                                 int64_t ldc, void* D, int64_t ldd, int32_t dtype, float alpha,
+                                 float beta, const void* bias, void* stream) {
+  const zcutlass::DType t = static_cast<zcutlass::DType>(dtype);
+  const zcutlass::layout::LayoutKind b_layout =
+      b_col_major ? zcutlass::layout::LayoutKind::ColumnMajor : zcutlass::layout::LayoutKind::RowMajor;
+  zcutlass::gemm_api::GemmArguments args{};
+  args.problem = {m, n, k};
+  args.A = {A, t, zcutlass::layout::LayoutKind::RowMajor, lda};
+  args.B = {B, t, b_layout, ldb};
+  args.C = {C, t, zcutlass::layout::LayoutKind::RowMajor, ldc};
+  args.D = {D, t, zcutlass::layout::LayoutKind::RowMajor, ldd};
+  args.alpha = alpha;
+  args.beta = beta;
+  args.bias = bias;
+  args.stream = static_cast<cudaStream_t>(stream);
+  const zcutlass::Status v = zcutlass::can_implement(args);
+  if (v != zcutlass::Status::Success) return static_cast<int>(v);
+  if (m == 0 || n == 0 || k == 0) return ZCUTLASS_SUCCESS;
+  zcb::LaunchArgs la{};
+  la.m = m;
+  la.n = n;
+  la.k = k;
+  la.a = A;
+  la.lda = lda;
+  la.b = B;
+  la.ldb = ldb;
+  la.c = beta != 0.0f ? C : nullptr;
+  la.ldc = ldc;
+  la.d = D;
+  la.ldd = ldd;
+  la.bias = bias;
+  la.alpha = alpha;
+  la.beta = beta;
+  la.bf16 = t == zcutlass::DType::BF16;
+  la.b_col_major = b_col_major != 0;
+  la.stream = static_cast<cudaStream_t>(stream);
+  return zcb::gemm_decode_noalloc(la);
+}
+
 }  // extern "C"

@@ -518,4 +518,118 @@ int selftest_bounded_wait(uint32_t timeout_us) {
   return read_and_clear_error_word(true);
 }
 
+// ---------------------------------------------------------------- decode without allocation
+//
+// Some callers cannot allocate device memory at call time (inside CUDA graph
+// capture, inside an allocator callback, or under a no-allocation-after-
+// start-up policy). For them the stream-K decode kernel can run with its
+// scratch -- tile counters and FP32 partial tiles -- in this fixed array
+// instead of the per-stream workspace. The array is part of the library
+// image: every device that loads the library holds it until exit.
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB
+constexpr size_t kNoAllocCounterBytes = size_t(64) << 10;   // 8192 tile counters
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+struct NoAllocSlot {
+  std::once_flag once;
+  void* ptr = nullptr;  // device address of g_noalloc_scratch on this device
+  cudaError_t err = cudaSuccess;
+};
+NoAllocSlot g_noalloc[kMaxDevices];
+
+template <typename T, int MP, int STAGES, bool KM>
+cudaError_t launch_swapab_sk_scratch_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit,
+                                       unsigned char* scratch) {
+  using L = swapab_sk::Smem<MP, STAGES, kDecodeKsub>;
+  CUtensorMap tw, tx;
+  const bool bf16 = a.bf16;
+  const bool w_ok =
+      KM ? make_tma_2d(&tw, a.b, bf16, a.n, a.k, a.ldb, swapab_sk::kBlockN, swapab_sk::kBlockK, TmaSwizzle::B128)
+         : make_tma_2d(&tw, a.b, bf16, a.k, a.n, a.ldb, swapab_sk::kBlockK, 64, TmaSwizzle::B128);
+  if (!w_ok || !make_tma_2d(&tx, a.a, bf16, a.m, a.k, a.lda, MP, swapab_sk::kBlockK, TmaSwizzle::B128)) {
+    return cudaErrorInvalidValue;
+  }
+  SwapAbSkParams p{};
+  p.m = static_cast<int>(a.m);
+  p.n = static_cast<int>(a.n);
+  p.k = static_cast<int>(a.k);
+  p.num_kb = static_cast<int>((a.k + kDecodeKBlock - 1) / kDecodeKBlock);
+  p.tiles_n = static_cast<int>((a.n + swapab_sk::kBlockN - 1) / swapab_sk::kBlockN);
+  p.total_units = static_cast<long long>(p.num_kb) * p.tiles_n;
+  p.grid = static_cast<int>(std::min<long long>(p.total_units, slot->info.sm_count));
+  p.alpha = a.alpha;
+  p.beta = a.beta;
+  p.c = a.c;
+  p.ldc = a.ldc;
+  p.d = a.d;
+  p.ldd = a.ldd;
+  p.bias = a.bias;
+  p.epi_flags = (a.beta != 0.0f ? kEpiHasC : 0u) | (a.bias != nullptr ? kEpiHasBias : 0u);
+  p.error_word = slot->info.error_word;
+  p.counters = reinterpret_cast<unsigned long long*>(scratch);
+  p.partials = reinterpret_cast<float*>(scratch + kNoAllocCounterBytes);
+  p.epoch = 1;
+  // The array keeps the previous call's counters: zero the ones this call uses.
+  cudaError_t e = cudaMemsetAsync(p.counters, 0, size_t(p.tiles_n) * sizeof(unsigned long long), a.stream);
+  if (e != cudaSuccess) return e;
+  auto kernel = swapab_sk::gemm_kernel<T, MP, STAGES, kDecodeKsub, KM>;
+  e = ensure_smem_attr(slot, config_bit, kernel, L::kDynamicBytes);
+  if (e != cudaSuccess) return e;
+  kernel<<<p.grid, swapab_sk::kThreads, L::kDynamicBytes, a.stream>>>(tw, tx, p);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return cudaGetLastError();
+}
+
+template <bool KM>
+cudaError_t launch_noalloc_km(const LaunchArgs& a, DeviceSlot* slot, unsigned char* scratch) {
+  const int off = KM ? kCfgColMajorB : 0;
+  if (a.m <= 16) {
+    return a.bf16 ? launch_swapab_sk_scratch_t<__nv_bfloat16, 16, 6, KM>(a, slot, kCfgSkBf16M16 + off, scratch)
+                  : launch_swapab_sk_scratch_t<half, 16, 6, KM>(a, slot, kCfgSkF16M16 + off, scratch);
+  }
+  if (a.m <= 32) {
+    return a.bf16 ? launch_swapab_sk_scratch_t<__nv_bfloat16, 32, 5, KM>(a, slot, kCfgSkBf16M32 + off, scratch)
+                  : launch_swapab_sk_scratch_t<half, 32, 5, KM>(a, slot, kCfgSkF16M32 + off, scratch);
+  }
+  return a.bf16 ? launch_swapab_sk_scratch_t<__nv_bfloat16, 64, 4, KM>(a, slot, kCfgSkBf16M64 + off, scratch)
+                : launch_swapab_sk_scratch_t<half, 64, 4, KM>(a, slot, kCfgSkF16M64 + off, scratch);
+}
+
+}  // namespace
+
+int gemm_decode_noalloc(const LaunchArgs& a) {
+  constexpr int kSuccess = 0, kInvalidArgument = 1, kRuntimeError = 3;
+  DeviceSlot* slot = current_slot();
+  if (slot == nullptr) return kRuntimeError;
+  if (slot->info.cc_major != 10 || slot->info.cc_minor != 0) return kInvalidArgument;
+  if (a.m < 1 || a.m > 64 || a.n > INT32_MAX || a.k > INT32_MAX) return kInvalidArgument;
+  if (!tma_compatible(a.a, a.lda) || !tma_compatible(a.b, a.ldb)) return kInvalidArgument;
+  // Size check before any device work.
+  const int mp = a.m <= 16 ? 16 : a.m <= 32 ? 32 : 64;
+  const long long tiles_n = (a.n + swapab_sk::kBlockN - 1) / swapab_sk::kBlockN;
+  const long long units = tiles_n * ((a.k + kDecodeKBlock - 1) / kDecodeKBlock);
+  const long long grid = std::min<long long>(units, slot->info.sm_count);
+  const size_t partial_bytes = size_t(2) * grid * mp * swapab_sk::kBlockN * sizeof(float);
+  if (size_t(tiles_n) * sizeof(unsigned long long) > kNoAllocCounterBytes ||
+      kNoAllocCounterBytes + partial_bytes > kNoAllocScratchBytes) {
+    return kInvalidArgument;
+  }
+  // Set-up, once per device with that device current: the host-side name of a
+  // __device__ array is not a device address, so look the address up.
+  NoAllocSlot& ns = g_noalloc[slot->info.ordinal];
+  std::call_once(ns.once, [&ns] {
+    ns.err = cudaGetSymbolAddress(&ns.ptr, g_noalloc_scratch);
+    if (ns.err == cudaSuccess && ns.ptr == nullptr) ns.err = cudaErrorInvalidSymbol;
+  });
+  if (ns.err != cudaSuccess) return kRuntimeError;
+  auto* scratch = static_cast<unsigned char*>(ns.ptr);
+  const cudaError_t e =
+      a.b_col_major ? launch_noalloc_km<true>(a, slot, scratch) : launch_noalloc_km<false>(a, slot, scratch);
+  return e == cudaSuccess ? kSuccess : kRuntimeError;
+}
+
 }  // namespace zcb

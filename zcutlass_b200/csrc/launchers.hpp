@@ -56,6 +56,10 @@ PersistentConfig choose_persistent(int64_t m, int64_t n, int sm_count);
 int swapab_choose_splits(int64_t n, int64_t k, int sm_count);
 
 int read_and_clear_error_word(bool clear);
+// Stream-K decode GEMM with its scratch in a fixed device array (no
+// allocation); returns a zcutlass status code. Arguments must already have
+// passed the generic validation.
+int gemm_decode_noalloc(const LaunchArgs& args);
 // Runs a kernel whose bounded mbarrier wait can never be satisfied; returns
 // the error code it recorded (expected non-zero), or -1 on a CUDA error.
 int selftest_bounded_wait(uint32_t timeout_us);
