@@ -1,12 +1,16 @@
 #!/usr/bin/env python3
 """Benchmark: Llama-3-8B-shaped prefill linears at TP = --gpus.
 
-One step = the four linears of one decoder layer at M = 8192 tokens, BF16:
-qkv [6144 x 4096] and gate_up [28672 x 4096] column-parallel (N split over
-ranks, no communication), o_proj [4096 x 4096] and down [4096 x 14336]
-row-parallel (K split, NCCL all-reduce of BF16 partials, chunked so the
-all-reduce overlaps the next GEMM chunk). 3573 GFLOP per step for the whole
-job, whatever the rank count (strong scaling).
+One step = the four linears of one decoder layer at M = 8192 tokens, BF16,
+in the layer's dependency order (qkv -> o_proj -> gate_up -> down; attention,
+norms and the activation are left out): qkv [6144 x 4096] and gate_up
+[28672 x 4096] column-parallel (N split over ranks, no communication),
+o_proj [4096 x 4096] and down [4096 x 14336] row-parallel (K split, then an
+all-reduce of the BF16 partials: the library's NVLS kernel, or NCCL with
+--comm nccl). At TP > 1 the 8192 tokens run as two independent 4096-row
+blocks on two streams (--micro), so one block's all-reduce overlaps the other
+block's GEMMs. 3573 GFLOP per step for the whole job, whatever the rank
+count (strong scaling).
 
     python bench.py                          # N=1, defaults
     torchrun --nproc-per-node N bench.py --gpus N --steps K --warmup W
@@ -131,10 +135,10 @@ def cpu_layer_sample(rows: int, dtype_name: str = "bf16"):
         "down": (torch.randn(S.hidden, S.intermediate, generator=g) * S.intermediate ** -0.5).to(dt),
     }
 
-    def step():
+    def step():  # the decoder layer's dependency order, as on the GPU
         qkv = overlay_fallback.linear(x, w["qkv"])
-        gu = overlay_fallback.linear(x, w["gate_up"])
-        overlay_fallback.linear(qkv[:, : S.o_in], w["o"])
+        o = overlay_fallback.linear(qkv[:, : S.o_in], w["o"])
+        gu = overlay_fallback.linear(o, w["gate_up"])
         return overlay_fallback.linear(gu[:, : S.intermediate], w["down"])
 
     return step, S.flops(rows)
@@ -238,7 +242,7 @@ def run_gpu(args) -> int:
     import torch.distributed as dist
 
     from zcutlass_b200 import _native, torch_ops
-    from zcutlass_b200.tp import LLAMA3_8B, TPDecoderLinears, TPGroup
+    from zcutlass_b200.tp import LLAMA3_8B, TPDecoderLinears, TPGroup, shard_range
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -255,6 +259,20 @@ def run_gpu(args) -> int:
     peaks, peaks_src = load_peaks()
     tp = TPGroup.from_env()
     layer = TPDecoderLinears(LLAMA3_8B, tp, device, torch.bfloat16, seed=0, chunks=args.chunks)
+    micro = args.micro if args.micro > 0 else (2 if world > 1 else 1)
+    comm = "none"
+    if world > 1:
+        want_nvls = args.comm == "nvls" or (args.comm == "auto" and world >= 4)
+        comm = "nvls" if want_nvls and layer.enable_nvls(TOKENS, lanes=micro) else "nccl"
+    streams = [torch.cuda.Stream(device) for _ in range(micro)] if micro > 1 else None
+    args.micro_used = micro
+
+    def step(xx, evs=None, outs=None):
+        """One layer step; returns (row offset, output block) pieces."""
+        if streams is not None:
+            ys = layer.forward_overlapped(xx, streams, outs)
+            return [(shard_range(xx.shape[0], j, micro)[0], y) for j, y in enumerate(ys)]
+        return [(0, layer.forward(xx, events=evs, out=None if outs is None else outs[0]))]
     g = torch.Generator(device="cpu").manual_seed(1)
     x_host = torch.randn(TOKENS, LLAMA3_8B.hidden, generator=g).to(torch.bfloat16)
     x = x_host.to(device)
@@ -272,8 +290,21 @@ def run_gpu(args) -> int:
         return float(t.item())
 
     for _ in range(args.warmup):
-        layer.forward(x)
+        step(x)
     barrier()
+    # At TP > 1 the step is replayed from a CUDA graph: its ~20 launches are
+    # host-bound otherwise (the GEMMs of a TP8 step last tens of microseconds).
+    use_graph = args.graph == "on" or (args.graph == "auto" and world > 1)
+    graph, launches_per_step = None, None
+    if use_graph:
+        graph = torch.cuda.CUDAGraph()
+        l0 = _native.kernel_launches()
+        with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+            step(x)
+        launches_per_step = _native.kernel_launches() - l0
+        for _ in range(3):
+            graph.replay()
+        barrier()
 
     # ---- device-timed steps (inputs resident in HBM)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -283,25 +314,44 @@ def run_gpu(args) -> int:
         barrier()
         start.record()
         for i in range(args.steps):
-            layer.forward(x, events={"gate_up": ev[i]})
+            if graph is not None:
+                graph.replay()
+            else:
+                step(x, {"gate_up": ev[i]})
         end.record()
         torch.cuda.synchronize()
     launches = _native.kernel_launches() - launches0
+    if graph is not None:  # replays launch what the capture recorded
+        launches = launches_per_step * args.steps
     ms = max_over_ranks(start.elapsed_time(end)) / args.steps
     barrier()
     total_flops = LLAMA3_8B.flops(TOKENS)
     value = total_flops / (ms * 1e-3) / 1e12
-    gate_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    live_gate = streams is None and graph is None
+    if live_gate:
+        gate_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
     gate_flops = 2.0 * TOKENS * layer.gate_up.weight.shape[0] * layer.gate_up.weight.shape[1]
-    gate_tflops = gate_flops / (gate_ms * 1e-3) / 1e12
     peak = peaks["bf16_tflops_sustained"]
+    # per-linear breakdown (untimed pass; o_proj and down include their all-reduce)
+    names = ("qkv", "gate_up", "o_proj", "down")
+    bev = [{nm: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for nm in names}
+           for _ in range(20)]
+    for evs in bev:
+        layer.forward(x, events=evs)
+    torch.cuda.synchronize()
+    breakdown = {nm: round(max_over_ranks(statistics.mean(e[nm][0].elapsed_time(e[nm][1]) for e in bev)), 4)
+                 for nm in names}
+    barrier()
+    if not live_gate:  # overlapped or graph-replayed steps: take gate_up from the sequential pass
+        gate_ms = statistics.mean(e["gate_up"][0].elapsed_time(e["gate_up"][1]) for e in bev)
+    gate_tflops = gate_flops / (gate_ms * 1e-3) / 1e12
     gw = layer.gate_up.weight
     gate_kernel = _native.selected_kernel(_native.make_desc(
         TOKENS, gw.shape[0], gw.shape[1], gw.shape[1], gw.shape[1], gw.shape[0], gw.shape[0], _native.BF16,
         b_layout=_native.COLUMN_MAJOR))["kernel_name"]
 
     # ---- end to end through the C ABI with pinned host buffers
-    e2e = run_e2e(args, layer, x_host, device, barrier, max_over_ranks, total_flops)
+    e2e = run_e2e(args, layer, step, x_host, device, barrier, max_over_ranks, total_flops, use_graph)
 
     line = None
     if rank == 0:
@@ -310,7 +360,10 @@ def run_gpu(args) -> int:
                "linears": {"qkv": [6144, 4096], "o_proj": [4096, 4096], "gate_up": [28672, 4096],
                            "down": [4096, 14336]},
                "l2": "inputs larger than L2 every step (436 MB of weights per layer at TP1), no flush",
-               "allreduce_chunks": args.chunks}
+               "allreduce": {"nvls": "zcutlass_nvls_allreduce (multimem.ld_reduce acc::f32 + multimem.st)",
+                             "nccl": f"NCCL all_reduce, {args.chunks} row chunks", "none": "none (TP1)"}[comm],
+               "micro_batches": micro, "cuda_graph": use_graph,
+               "order": "qkv -> o_proj (+all-reduce) -> gate_up -> down (+all-reduce)"}
         sm = clocks.summary()
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
@@ -320,6 +373,8 @@ def run_gpu(args) -> int:
             "per_gpu_tflops": round(value / world, 2),
             "frac_of_bf16_peak_per_gpu": round(value / world / peak, 4),
             "roofline": {"bound": "tensor", "kernel": f"gate_up ({gate_kernel})",
+                         "timing": "events around gate_up in the timed steps" if live_gate else
+                                   "events around gate_up in a sequential pass after the timed steps",
                          "achieved": round(gate_tflops, 2), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(gate_tflops / peak, 4),
                          "peak_source": f"bf16_tflops_sustained of {peaks_src} (burst {peaks['bf16_tflops']})",
@@ -327,6 +382,7 @@ def run_gpu(args) -> int:
                          "algorithmic_flops_per_launch": gate_flops, "avg_launch_ms": round(gate_ms, 4),
                          "traffic": GATE_UP_TRAFFIC_BYTES},
             "clocks": sm,
+            "linear_ms": breakdown,
             "e2e": e2e,
             "gpu_launches": launches,
         }
@@ -338,12 +394,14 @@ def run_gpu(args) -> int:
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
+        graph = None  # release the captured graph (it may hold NCCL calls) first
+        torch.cuda.synchronize()
         barrier()
         dist.destroy_process_group()
     return 0
 
 
-def run_e2e(args, layer, x_host, device, barrier, max_over_ranks, total_flops) -> dict:
+def run_e2e(args, layer, step, x_host, device, barrier, max_over_ranks, total_flops, use_graph=False) -> dict:
     """Same step with host buffers, whole job copying the input once and the
     output once: rank r copies rows [r0, r1) of the layer input from pinned
     host memory (H2D stream), an NCCL all-gather over NVLink assembles the
@@ -364,11 +422,29 @@ def run_e2e(args, layer, x_host, device, barrier, max_over_ranks, total_flops) -
     dx_part = [torch.empty_like(hx, device=device) for _ in range(2)]
     dx = dx_part if world == 1 else [torch.empty(m, hidden, device=device, dtype=hx.dtype) for _ in range(2)]
     dout = [torch.empty(m, layer.shape.hidden, device=device, dtype=hx.dtype) for _ in range(2)]
+    res = [None, None]
+    streams_n = args.micro_used
+    blocks = [shard_range(m, j, streams_n) for j in range(streams_n)]
     hout = [torch.empty(r1 - r0, layer.shape.hidden, dtype=hx.dtype).pin_memory() for _ in range(2)]
     e = lambda: torch.cuda.Event()  # noqa: E731
     h2d_ev, d2h_ev, comp_ev = [e(), e()], [e(), e()], [e(), e()]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     steps = args.steps
+
+    def compute_part(s):
+        if world > 1:
+            dist.all_gather_into_tensor(dx[s], dx_part[s], group=layer.tp.group)
+        # NVLS keeps the output in its lanes' ping-pong symmetric buffers
+        return step(dx[s], outs=None if layer.down.nvls else [dout[s]] if streams_n == 1 else
+                    [dout[s][p0:p1] for p0, p1 in blocks])
+
+    graphs, graph_res = [], []
+
+    def run_compute(s):
+        if graphs:
+            graphs[s].replay()
+            return graph_res[s]
+        return compute_part(s)
 
     def loop(n):
         start.record(compute)
@@ -381,9 +457,7 @@ def run_e2e(args, layer, x_host, device, barrier, max_over_ranks, total_flops) -
             compute.wait_event(h2d_ev[s])
             if i >= 2:
                 compute.wait_event(d2h_ev[s])
-            if world > 1:
-                dist.all_gather_into_tensor(dx[s], dx_part[s], group=layer.tp.group)
-            layer.forward(dx[s], out=dout[s])
+            res[s] = run_compute(s)
             comp_ev[s].record(compute)
             if i + 1 < n:
                 if i >= 1:
@@ -393,7 +467,10 @@ def run_e2e(args, layer, x_host, device, barrier, max_over_ranks, total_flops) -
                 h2d_ev[1 - s].record(h2d_s)
             d2h_s.wait_event(comp_ev[s])
             with torch.cuda.stream(d2h_s):
-                hout[s].copy_(dout[s][r0:r1], non_blocking=True)
+                for p0, y in res[s]:  # this rank's rows [r0, r1) from each output block
+                    lo, hi = max(r0, p0), min(r1, p0 + y.shape[0])
+                    if lo < hi:
+                        hout[s][lo - r0:hi - r0].copy_(y[lo - p0:hi - p0], non_blocking=True)
             d2h_ev[s].record(d2h_s)
         compute.wait_event(d2h_ev[(n - 1) % 2])
         end.record(compute)
@@ -401,9 +478,19 @@ def run_e2e(args, layer, x_host, device, barrier, max_over_ranks, total_flops) -
 
     loop(min(3, steps))
     barrier()
+    if use_graph:  # one graph per input/output buffer pair (the copies stay outside)
+        for s in range(2):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                graph_res.append(compute_part(s))
+            graphs.append(g)
+        loop(min(3, steps))
+        barrier()
     loop(steps)
     ms = max_over_ranks(start.elapsed_time(end)) / steps
     barrier()
+    graphs.clear()  # graphs holding NCCL calls go before the process group does
+    torch.cuda.synchronize()
     return {"value": round(total_flops / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
             "h2d_bytes_per_step": m * hidden * hx.element_size(),
             "d2h_bytes_per_step": m * layer.shape.hidden * hx.element_size(),
@@ -417,7 +504,14 @@ def main(argv=None) -> int:
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["zcutlass", "reference"], default="zcutlass")
-    ap.add_argument("--chunks", type=int, default=4, help="row chunks of the row-parallel all-reduce")
+    ap.add_argument("--chunks", type=int, default=1, help="row chunks of the NCCL row-parallel all-reduce")
+    ap.add_argument("--micro", type=int, default=0,
+                    help="independent row blocks per step, each on its own stream (0: 2 when TP > 1, else 1)")
+    ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",
+                    help="replay each step from a CUDA graph (auto: when TP > 1)")
+    ap.add_argument("--comm", choices=["auto", "nvls", "nccl"], default="auto",
+                    help="row-parallel all-reduce: the library's NVLS kernel or NCCL (auto: NVLS from TP4 up; "
+                         "at TP2 NVLS moves 1.5x the bytes of a ring and NCCL is faster)")
     ap.add_argument("--skip-decode", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     args = ap.parse_args(argv)

@@ -23,6 +23,8 @@
  *                               tcgen05 kernels set when a bounded wait expires
  *   zcutlass_gemm_kernel_launches  number of kernel launches this library made
  *   zcutlass_selftest_bounded_wait runs a kernel whose bounded wait must expire
+ *   zcutlass_gemm_decode_noalloc   decode GEMM that allocates nothing
+ *   zcutlass_nvls_allreduce     row-parallel all-reduce over NVLink SHARP
  *
  * Integer enum values equal the C++ enum values (Status, DType, LayoutKind).
  * Return values of type int that carry a status use zcutlass_status values.
@@ -138,6 +140,28 @@ int zcutlass_gemm_decode_noalloc(int64_t m, int64_t n, int64_t k, const void* A,
                                  const void* B, int64_t ldb, int32_t b_col_major, const void* C,
                                  int64_t ldc, void* D, int64_t ldd, int32_t dtype, float alpha,
                                  float beta, const void* bias, void* stream);
+
+/* Tensor-parallel all-reduce over NVLink SHARP (no reference counterpart: the
+ * reference leaves the row-parallel all-reduce to vLLM/NCCL). Sums, in place,
+ * `nbytes` (a multiple of 16) of f16/bf16 held at the same offset of a
+ * symmetric buffer on every rank; `mc_ptr` is that data's multicast address
+ * (16-byte aligned). Rank `rank` reduces its 1/world slice with FP32
+ * accumulation in the switch and broadcasts it.
+ *
+ * The call brackets the reduction with two cross-rank barriers of its own
+ * (every partial written before; every slice written after), kept in two
+ * uint32 words of symmetric memory (8-byte aligned): `flag` is their local
+ * address, `mc_flag` the multicast address of the first. Both words must be
+ * 0 on every rank before the first call; word 0 counts arrivals from all
+ * ranks, word 1 this rank's barriers. Calls that share the words must run in
+ * one stream order on each rank, and every rank of the group must make the
+ * same calls in the same order. The launches take no per-call state from the
+ * host, so they may be captured in a CUDA graph and replayed. A barrier that
+ * waits longer than two seconds gives up and sets the device error word
+ * (zcutlass_device_error) instead of hanging.
+ * Asynchronous on `stream` (three kernel launches). */
+int zcutlass_nvls_allreduce(void* mc_ptr, int64_t nbytes, int32_t dtype, void* mc_flag, void* flag,
+                            int32_t rank, int32_t world, void* stream);
 
 /* Failure-detection self test (no reference counterpart): launches one kernel
  * whose bounded mbarrier wait is never satisfied, with a limit of `timeout_us`

@@ -92,6 +92,9 @@ def _worker_sharding(rank, world, port, errq):
         wd = gather(layer.down.weight, 1)
         torch.testing.assert_close(out, d_in @ wd.t(), rtol=1e-4, atol=1e-4)
         torch.testing.assert_close(layer.buffers(6, "cpu", torch.float32)["o"], o_in @ wo.t(), rtol=1e-4, atol=1e-4)
+        # gate_up consumes the all-reduced o_proj output (the layer's dependency order)
+        bufs = layer.buffers(6, "cpu", torch.float32)
+        torch.testing.assert_close(bufs["gate_up"], bufs["o"] @ layer.gate_up.weight.t(), rtol=1e-4, atol=1e-4)
         assert qkv_full.shape == (6, shape.qkv_out) and gu_full.shape == (6, 2 * shape.intermediate)
         assert layer.flops_per_rank(6) > 0
         dist.barrier()

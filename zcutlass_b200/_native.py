@@ -88,6 +88,8 @@ SIGNATURES = {
     "zcutlass_device_error": (ctypes.c_int, [ctypes.c_int]),
     "zcutlass_gemm_kernel_launches": (ctypes.c_uint64, []),
     "zcutlass_selftest_bounded_wait": (ctypes.c_int, [ctypes.c_uint32]),
+    "zcutlass_nvls_allreduce": (ctypes.c_int, [_v, _i64, ctypes.c_int32, _v, _v, ctypes.c_int32, ctypes.c_int32,
+                                               _v]),
     "zcutlass_gemm_decode_noalloc": (ctypes.c_int, [_i64, _i64, _i64, _v, _i64, _v, _i64, ctypes.c_int32, _v, _i64,
                                                     _v, _i64, ctypes.c_int32, ctypes.c_float, ctypes.c_float, _v,
                                                     _v]),

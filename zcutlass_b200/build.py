@@ -36,7 +36,7 @@ CXX = os.environ.get("CXX", "g++")
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 CORE_HOST_SRCS = ["foundation.cpp", "gemm.cpp", "c_abi.cpp", "tma_desc.cpp"]
-CORE_CUDA_SRCS = ["launchers.cu"]
+CORE_CUDA_SRCS = ["launchers.cu", "collectives.cu"]
 
 
 def _headers() -> list[Path]:

@@ -117,6 +117,16 @@ uint64_t zcutlass_gemm_kernel_launches(void) { return zcb::launch_count(); }
 
 int zcutlass_selftest_bounded_wait(uint32_t timeout_us) { return zcb::selftest_bounded_wait(timeout_us); }
 
+int zcutlass_nvls_allreduce(void* mc_ptr, int64_t nbytes, int32_t dtype, void* mc_flag, void* flag, int32_t rank,
+                            int32_t world, void* stream) {
+  if (dtype != ZCUTLASS_F16 && dtype != ZCUTLASS_BF16) return ZCUTLASS_NOT_SUPPORTED;
+  const cudaError_t e = zcb::launch_nvls_allreduce(mc_ptr, nbytes, dtype == ZCUTLASS_BF16,
+                                                   static_cast<uint32_t*>(mc_flag), static_cast<uint32_t*>(flag), rank,
+                                                   world, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ZCUTLASS_SUCCESS
+                          : (e == cudaErrorInvalidValue ? ZCUTLASS_INVALID_ARGUMENT : ZCUTLASS_RUNTIME_ERROR);
+}
+
 // For callers that may not allocate device memory at call time (see the
 // header): same validation as zcutlass_gemm, then the stream-K decode kernel
 // with its scratch in the library's fixed device array.

@@ -75,7 +75,7 @@ struct WaitCtx {
   uint64_t timeout_ns = kWaitTimeoutNs;
 };
 
-__device__ __noinline__ void report_wait_timeout(const WaitCtx& ctx, int code) {
+static __device__ __noinline__ void report_wait_timeout(const WaitCtx& ctx, int code) {
   *ctx.abort_flag = 1;
   if (ctx.error_word != nullptr) atomicCAS(ctx.error_word, 0, code);
 }

@@ -491,6 +491,7 @@ int read_and_clear_error_word(bool clear) {
 }
 
 uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
+void count_launches(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 // One thread waits on an mbarrier that nothing ever arrives on, with the same
 // bounded wait the GEMM kernels use but a caller-chosen limit. The wait must

@@ -55,6 +55,13 @@ enum class PersistentConfig { Pair256x256, Cta128x256, Cta128x128 };
 PersistentConfig choose_persistent(int64_t m, int64_t n, int sm_count);
 int swapab_choose_splits(int64_t n, int64_t k, int sm_count);
 
+// In-place NVLS all-reduce (sum) of `nbytes` of f16/bf16 at multicast
+// address `mc_ptr` (collectives.cu): barrier, each rank reduces and
+// broadcasts its slice, barrier. The barriers use two symmetric u32 words:
+// flag[0] the cross-rank counter (multicast address `mc_flag`), flag[1] this
+// rank's barrier count.
+cudaError_t launch_nvls_allreduce(void* mc_ptr, int64_t nbytes, bool bf16, uint32_t* mc_flag, uint32_t* flag,
+                                  int rank, int world, cudaStream_t stream);
 int read_and_clear_error_word(bool clear);
 // Stream-K decode GEMM with its scratch in a fixed device array (no
 // allocation); returns a zcutlass status code. Arguments must already have
@@ -64,5 +71,6 @@ int gemm_decode_noalloc(const LaunchArgs& args);
 // the error code it recorded (expected non-zero), or -1 on a CUDA error.
 int selftest_bounded_wait(uint32_t timeout_us);
 uint64_t launch_count();
+void count_launches(uint64_t n);
 
 }  // namespace zcb

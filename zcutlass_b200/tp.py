@@ -8,9 +8,16 @@ vLLM. This module provides the same two shardings natively:
   column-parallel (qkv, gate_up): weight rows (output features) split across
       ranks; every rank computes its slice of the output, no communication.
   row-parallel (o_proj, down): weight columns (input features) split across
-      ranks; every rank computes a full-size BF16/F16 partial, then an NCCL
-      all-reduce (sum) over NVLink combines them. The GEMM is issued in row
-      chunks so the all-reduce of chunk i overlaps the GEMM of chunk i+1.
+      ranks; every rank computes a full-size BF16/F16 partial, then an
+      all-reduce (sum) over NVLink combines them: the library's own NVLS
+      kernel (multimem reduction in the NVSwitch, FP32 accumulation) on
+      symmetric memory when the node supports multicast, else NCCL with the
+      GEMM issued in row chunks so the all-reduce of chunk i overlaps the
+      GEMM of chunk i+1.
+
+TPDecoderLinears chains the four linears of one decoder layer;
+forward_overlapped() runs independent row blocks on separate streams so one
+block's all-reduce overlaps another block's GEMMs.
 
 Weights use the PyTorch [out_features, in_features] layout and go to the
 kernels as column-major B (no transposed copy). Every GEMM runs through the
@@ -91,11 +98,84 @@ class ColumnParallelLinear:
     __call__ = forward
 
 
+class NvlsReducer:
+    """Row-parallel outputs in symmetric memory with an NVLink SHARP mapping.
+
+    Two symmetric buffers alternate between calls (the consumer of call i can
+    still be reading buffer i while call i+1 writes the other). `reduce`
+    sums a partial in place across ranks with the library's NVLS all-reduce
+    (zcutlass_nvls_allreduce: FP32 accumulation in the switch, one NVLink
+    crossing per byte and direction), which brackets the reduction with its
+    own bounded cross-rank barriers on two counter words kept in the same
+    symmetric allocation, after the two buffers. Every launch is fixed at
+    issue time (no per-call values), so a step can be captured in a CUDA
+    graph; each replay then alternates nothing -- the buffer a captured call
+    uses is the one it used at capture."""
+
+    def __init__(self, max_rows: int, cols: int, dtype, device, group=None) -> None:
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+
+        group = group or dist.group.WORLD
+        self.dtype = dtype
+        elem = torch.empty(0, dtype=dtype).element_size()
+        region = -(-max_rows * cols * elem // 256) * 256
+        raw = symm.empty(2 * region + 256, dtype=torch.uint8, device=device)
+        self.handle = symm.rendezvous(raw, group)
+        if not self.handle.multicast_ptr:
+            raise RuntimeError("NVLS multicast is not available for this group")
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.raw = raw
+        self.bufs = [raw[i * region: i * region + max_rows * cols * elem].view(dtype).view(max_rows, cols)
+                     for i in range(2)]
+        # multicast address = multicast base + offset of the local address in the allocation
+        self.mc_base = self.handle.multicast_ptr - self.handle.buffer_ptrs[self.rank]
+        self.flag = raw.data_ptr() + 2 * region
+        raw[2 * region:].zero_()  # barrier counter and barrier count
+        self.turn = 0
+        torch.cuda.synchronize(device)
+        dist.barrier(group)
+
+    last_error: str | None = None  # why the last try_create returned None
+
+    @classmethod
+    def try_create(cls, *args, **kwargs):
+        """The reducer, or None when the group has no multicast support."""
+        try:
+            return cls(*args, **kwargs)
+        except Exception as exc:  # no symmetric memory / no NVLS on this node
+            cls.last_error = f"{type(exc).__name__}: {exc}"
+            return None
+
+    def next_buffer(self, rows: int):
+        i = self.turn
+        self.turn ^= 1
+        return i, self.bufs[i][:rows]
+
+    def reduce(self, i: int, rows: int) -> None:
+        import torch
+
+        from . import _native
+
+        t = self.bufs[i]
+        nbytes = rows * t.shape[1] * t.element_size()
+        st = _native.lib().zcutlass_nvls_allreduce(
+            self.mc_base + t.data_ptr(), nbytes, _native.BF16 if self.dtype == torch.bfloat16 else _native.F16,
+            self.mc_base + self.flag, self.flag, self.rank, self.world, torch.cuda.current_stream().cuda_stream)
+        if st != _native.SUCCESS:
+            raise RuntimeError(f"zcutlass_nvls_allreduce failed: {_native.status_name(st)}")
+
+
 class RowParallelLinear:
     """y = all_reduce_sum(x_shard @ W_shard^T) + b; W_shard = W[:, cols owned by this rank].
 
     The bias is added once, by rank 0's partial, so the all-reduced sum carries
-    it exactly once. `chunks` row blocks let NCCL overlap with the GEMM."""
+    it exactly once. Over NCCL, `chunks` row blocks let the all-reduce of one
+    block overlap the GEMM of the next. With enable_nvls() the partial goes
+    into symmetric memory and the library's NVLS all-reduce sums it in place;
+    each `lane` (a stream that runs its own chain of layers concurrently with
+    the others) then has its own buffers and barrier word."""
 
     def __init__(self, weight_shard, bias=None, tp: TPGroup | None = None, chunks: int = 4,
                  linear_fn=None) -> None:
@@ -104,6 +184,30 @@ class RowParallelLinear:
         self.tp = tp or TPGroup()
         self.chunks = max(1, chunks)
         self.linear_fn = linear_fn or _linear_into
+        self.nvls_lanes: list[NvlsReducer] = []  # set by enable_nvls()
+
+    @property
+    def nvls(self) -> "NvlsReducer | None":
+        return self.nvls_lanes[0] if self.nvls_lanes else None
+
+    def enable_nvls(self, max_rows: int, lanes: int = 1) -> bool:
+        """Switch the all-reduce from NCCL to the library's NVLS kernel (if the
+        group supports multicast), with `lanes` independent buffer sets of
+        `max_rows` rows; returns whether it is active."""
+        import torch
+        import torch.distributed as dist
+
+        if self.tp.world_size > 1 and len(self.nvls_lanes) < lanes:
+            made = [NvlsReducer.try_create(max_rows, self.weight.shape[0], self.weight.dtype,
+                                           self.weight.device, self.tp.group)
+                    for _ in range(lanes - len(self.nvls_lanes))]
+            # every rank must take the same path: use NVLS only if all ranks have it
+            ok = torch.tensor([0 if any(r is None for r in made) else 1], device=self.weight.device,
+                              dtype=torch.int32)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.tp.group)
+            if int(ok.item()) == 1:
+                self.nvls_lanes.extend(made)
+        return len(self.nvls_lanes) >= lanes
 
     @classmethod
     def from_full(cls, weight, bias=None, tp: TPGroup | None = None, chunks: int = 4,
@@ -112,14 +216,26 @@ class RowParallelLinear:
         lo, hi = shard_range(weight.shape[1], tp.rank, tp.world_size)
         return cls(weight[:, lo:hi].contiguous(), bias, tp, chunks, linear_fn)
 
-    def forward(self, x_shard, out=None):
+    def forward(self, x_shard, out=None, lane: int = 0):
+        """The all-reduced output. With NVLS and no `out` it is a view of the
+        lane's symmetric buffer, valid until the lane's second-next call."""
         import torch
         import torch.distributed as dist
 
         m = x_shard.shape[0]
+        bias = self.bias if self.tp.rank == 0 else None
+        if self.nvls_lanes and self.tp.world_size > 1:
+            red = self.nvls_lanes[lane]
+            # partial into local symmetric memory, then the NVLS all-reduce in place
+            i, y = red.next_buffer(m)
+            self.linear_fn(x_shard, self.weight, bias, y)
+            red.reduce(i, m)
+            if out is not None:
+                out.copy_(y)
+                return out
+            return y
         if out is None:
             out = torch.empty(m, self.weight.shape[0], device=x_shard.device, dtype=x_shard.dtype)
-        bias = self.bias if self.tp.rank == 0 else None
         if self.tp.world_size == 1:
             self.linear_fn(x_shard, self.weight, bias, out)
             return out
@@ -200,6 +316,10 @@ class TPDecoderLinears:
         self.d_cols = d_hi - d_lo
         self._bufs = {}
 
+    def enable_nvls(self, max_tokens: int, lanes: int = 1) -> bool:
+        """Use the library's NVLS all-reduce for both row-parallel linears."""
+        return self.o_proj.enable_nvls(max_tokens, lanes) and self.down.enable_nvls(max_tokens, lanes)
+
     def flops_per_rank(self, tokens: int) -> float:
         q = self.qkv.weight.shape[0] * self.qkv.weight.shape[1]
         gu = self.gate_up.weight.shape[0] * self.gate_up.weight.shape[1]
@@ -207,10 +327,10 @@ class TPDecoderLinears:
         d = self.down.weight.shape[0] * self.down.weight.shape[1]
         return 2.0 * tokens * (q + gu + o + d)
 
-    def buffers(self, tokens: int, device, dtype) -> dict:
+    def buffers(self, tokens: int, device, dtype, lane: int = 0) -> dict:
         import torch
 
-        key = (tokens, str(device), dtype)
+        key = (tokens, str(device), dtype, lane)
         if key not in self._bufs:
             e = lambda *s: torch.empty(*s, device=device, dtype=dtype)  # noqa: E731
             self._bufs[key] = {
@@ -221,11 +341,11 @@ class TPDecoderLinears:
             }
         return self._bufs[key]
 
-    def forward(self, x, events: dict | None = None, out=None):
-        """x: [tokens, hidden] (replicated on every rank). Returns the down output
-        (written into `out` when given). `events` (optional) maps a GEMM name to
-        a (start, end) CUDA event pair recorded around that GEMM on the current stream."""
-        b = self.buffers(x.shape[0], x.device, x.dtype)
+    def _steps(self, x, lane: int, out, events: dict | None):
+        """The chain for one block of tokens, as two callables: up to and
+        including o_proj's all-reduce, then gate_up, down and its all-reduce."""
+        b = self.buffers(x.shape[0], x.device, x.dtype, lane)
+        state = {}
 
         def timed(name, fn):
             if events is not None and name in events:
@@ -235,11 +355,54 @@ class TPDecoderLinears:
                 return r
             return fn()
 
-        timed("qkv", lambda: self.qkv(x, b["qkv"]))
-        timed("gate_up", lambda: self.gate_up(x, b["gate_up"]))
-        # o_proj input: this rank's slice of attention output, stood in by the q part of qkv.
-        o_in = b["qkv"][:, : self.o_cols]
-        timed("o_proj", lambda: self.o_proj(o_in, b["o"]))
-        # down input: this rank's slice of act(gate) * up, stood in by the gate_up output.
-        d_in = b["gate_up"][:, : self.d_cols]
-        return timed("down", lambda: self.down(d_in, b["down"] if out is None else out))
+        def first():
+            timed("qkv", lambda: self.qkv(x, b["qkv"]))
+            # o_proj input: this rank's heads of the attention output, stood in by the q part of qkv
+            o_in = b["qkv"][:, : self.o_cols]
+            # with NVLS the row-parallel outputs stay in their symmetric buffers (no copy)
+            state["o"] = timed("o_proj", lambda: self.o_proj(o_in, None if self.o_proj.nvls else b["o"], lane))
+
+        def second():
+            # gate_up consumes the all-reduced o_proj output (the residual + norm step is left out)
+            timed("gate_up", lambda: self.gate_up(state["o"], b["gate_up"]))
+            # down input: this rank's slice of act(gate) * up, stood in by the gate_up output
+            d_in = b["gate_up"][:, : self.d_cols]
+            dst = out if out is not None or self.down.nvls is not None else b["down"]
+            state["y"] = timed("down", lambda: self.down(d_in, dst, lane))
+
+        return first, second, state
+
+    def forward(self, x, events: dict | None = None, out=None):
+        """x: [tokens, hidden] (replicated on every rank). Runs the four GEMMs in
+        a decoder layer's dependency order -- qkv, o_proj (+ all-reduce), gate_up
+        on the o_proj output, down (+ all-reduce) -- and returns the down output
+        (written into `out` when given). `events` (optional) maps a GEMM name to
+        a (start, end) CUDA event pair recorded around that GEMM on the current stream."""
+        first, second, state = self._steps(x, 0, out, events)
+        first()
+        second()
+        return state["y"]
+
+    def forward_overlapped(self, x, streams, outs=None):
+        """The same layer over len(streams) independent blocks of rows of x (as
+        from different sequences), each block's chain on its own stream and
+        NVLS lane, issued interleaved so one block's all-reduce overlaps the
+        next block's GEMMs. Returns the per-block down outputs (row blocks of
+        x in order); `outs` optionally gives their destinations."""
+        import torch
+
+        n = len(streams)
+        cur = torch.cuda.current_stream(x.device)
+        chains = []
+        for j in range(n):
+            r0, r1 = shard_range(x.shape[0], j, n)
+            chains.append(self._steps(x[r0:r1], j, None if outs is None else outs[j], None))
+        for s in streams:
+            s.wait_stream(cur)
+        for phase in (0, 1):
+            for j, s in enumerate(streams):
+                with torch.cuda.stream(s):
+                    chains[j][phase]()
+        for s in streams:
+            cur.wait_stream(s)
+        return [c[2]["y"] for c in chains]
