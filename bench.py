@@ -42,10 +42,11 @@ METRIC = "Prefill GEMM TFLOP/s/GPU (% of BF16 dense peak) at TP 1/2/4/8; decode 
 TOKENS = 8192
 MEASURED_PEAKS = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# DRAM traffic per launch of the dominant kernel (gate_up, 128x256 persistent
-# tcgen05 kernel) from one ncu capture; see profiles/ for the capture and the
-# scaling from the captured case. None until a capture exists.
-GATE_UP_TRAFFIC_BYTES = None
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
+# the dominant kernel at TP1 -- gate_up 8192 x 28672 x 4096 on the 2-CTA
+# 256x256 kernel -- from one ncu capture of that exact launch (1183.8 MB read +
+# 457.6 MB written; algorithmic 301.9 MB read + 469.8 MB written).
+GATE_UP_TRAFFIC_BYTES = 1183789568 + 457606400
 
 NVML_REASONS = {
     0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
@@ -380,7 +381,7 @@ def run_gpu(args) -> int:
                          "peak_source": f"bf16_tflops_sustained of {peaks_src} (burst {peaks['bf16_tflops']})",
                          "frac_of_burst": round(gate_tflops / peaks["bf16_tflops"], 4),
                          "algorithmic_flops_per_launch": gate_flops, "avg_launch_ms": round(gate_ms, 4),
-                         "traffic": GATE_UP_TRAFFIC_BYTES},
+                         "traffic": GATE_UP_TRAFFIC_BYTES if world == 1 else None},
             "clocks": sm,
             "linear_ms": breakdown,
             "e2e": e2e,

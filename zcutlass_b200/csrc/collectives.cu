@@ -85,10 +85,16 @@ __device__ __forceinline__ void multimem_st(uint8_t* addr, const uint4& v) {
   }
 }
 
-// 256 threads x 8 reductions in flight: 32 KiB outstanding per block with few
-// registers, so a block fits on an SM beside a persistent GEMM CTA.
+// Launch shape, from a sweep of threads x unroll x blocks at 8 ranks: with
+// 32 MiB / 64 MiB, reduction alone or broadcast alone each runs at ~560 GB/s
+// per GPU whatever the shape, but run together they contend in the switch
+// and the time grows with the number of blocks (64 MiB: 160 us at 16-32
+// blocks, 205 us at 256). 32 blocks x 256 threads x 4 reductions in flight
+// (16 KiB outstanding per block) is at the minimum, and leaves the other
+// SMs to a concurrently running GEMM.
 constexpr int kArThreads = 256;
-constexpr int kArUnroll = 8;
+constexpr int kArUnroll = 4;
+constexpr int kArMaxBlocks = 32;
 
 template <bool kBf16>
 __global__ void __launch_bounds__(kArThreads) nvls_allreduce_kernel(uint8_t* mc, int64_t words16, int rank,
@@ -147,11 +153,10 @@ cudaError_t launch_nvls_allreduce(void* mc_ptr, int64_t nbytes, bool bf16, uint3
   if (info == nullptr) return cudaErrorInvalidDevice;
   const cudaError_t ce = ensure_carveout(info->ordinal);
   if (ce != cudaSuccess) return ce;
-  const int sms = info->sm_count > 0 ? info->sm_count : 148;
   const int64_t words = nbytes / 16;
   const int64_t per_rank = (words + world - 1) / world;
   const int64_t per_block = static_cast<int64_t>(kArThreads) * kArUnroll;
-  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((per_rank + per_block - 1) / per_block, 2 * sms));
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((per_rank + per_block - 1) / per_block, kArMaxBlocks));
   const uint32_t w = static_cast<uint32_t>(world);
 
   nvls_barrier_kernel<<<1, 32, 0, stream>>>(mc_flag, flag, w, kWaitTimeoutNs, kErrNvlsBarrierPre, info->error_word);
