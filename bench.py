@@ -197,14 +197,15 @@ def run_reference(args) -> int:
 
 def decode_sweep(device, peaks: dict, iters: int = 200) -> list[dict]:
     """Llama-3-70B TP=8 per-GPU decode linears on one GPU:
-    achieved HBM GB/s, weights rotated over > 2x L2 so every launch streams HBM."""
+    achieved HBM GB/s, weights rotated over > 2x L2 so every launch streams HBM.
+    The `iters` launches are captured once in a CUDA graph and replayed, as a
+    decode step is in serving, so the time is the kernels' and not the host's."""
     import torch
 
     from zcutlass_b200 import _native
 
     shapes = {"qkv": (1280, 8192), "o_proj": (8192, 1024), "gate_up": (7168, 8192), "down": (8192, 3584)}
     out = []
-    stream = torch.cuda.current_stream(device).cuda_stream
     for name, (n, k) in shapes.items():
         wbytes = n * k * 2
         copies = max(2, -(-3 * 126 * 2**20 // wbytes))
@@ -212,26 +213,37 @@ def decode_sweep(device, peaks: dict, iters: int = 200) -> list[dict]:
         for m in (1, 8, 16, 32):
             x = torch.randn(m, k, device=device, dtype=torch.bfloat16)
             d = torch.empty(m, n, device=device, dtype=torch.bfloat16)
-            descs = [_native.make_desc(m, n, k, k, k, n, n, _native.BF16, stream=stream,
-                                       b_layout=_native.COLUMN_MAJOR) for _ in ws]
 
-            def run(i):
+            def run(i, descs):
                 st = _native.gemm(descs[i % copies], x.data_ptr(), ws[i % copies].data_ptr(), None, d.data_ptr())
                 assert st == 0, st
 
+            def make_descs():
+                stream = torch.cuda.current_stream(device).cuda_stream
+                return [_native.make_desc(m, n, k, k, k, n, n, _native.BF16, stream=stream,
+                                          b_layout=_native.COLUMN_MAJOR) for _ in ws]
+
+            eager = make_descs()
             for i in range(2 * copies):
-                run(i)
+                run(i, eager)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+                captured = make_descs()
+                for i in range(iters):
+                    run(i, captured)
+            graph.replay()
             torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            for i in range(iters):
-                run(i)
+            graph.replay()
             e1.record()
             torch.cuda.synchronize()
+            del graph
             us = e0.elapsed_time(e1) * 1e3 / iters
             nbytes = 2 * (m * k + n * k + m * n)
             gbs = nbytes / (us * 1e-6) / 1e9
-            sel = _native.selected_kernel(descs[0])["kernel_name"]
+            sel = _native.selected_kernel(eager[0])["kernel_name"]
             out.append({"linear": name, "m": m, "n": n, "k": k, "us": round(us, 2), "GB/s": round(gbs, 1),
                         "frac_hbm": round(gbs / peaks["hbm_gbs"], 3), "kernel": sel})
         del ws

@@ -41,6 +41,10 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GenericGemmParams 
   const T* C = static_cast<const T*>(p.c);
   const T* bias = static_cast<const T*>(p.bias);
   T* D = static_cast<T*>(p.d);
+  // Launched with programmatic stream serialization: wait for the previous
+  // kernel on the stream before touching global memory.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const int64_t tiles_m = (p.m + kTile - 1) / kTile;
 

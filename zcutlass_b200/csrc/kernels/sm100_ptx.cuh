@@ -30,6 +30,21 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 
 __device__ __forceinline__ bool elect_lane0() { return (threadIdx.x & 31) == 0; }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialization may start while the previous kernel on its stream is still
+// running; griddep_wait() returns once that kernel has completed and its
+// memory operations are visible, so every global access comes after it (it
+// returns at once when the launch had no such dependency).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Allows the next kernel on the stream, if launched with the attribute, to
+// begin its prologue. The tcgen05 kernels call it only after their TMEM is
+// allocated, so a dependent CTA can never hold TMEM columns that a not yet
+// started CTA of this grid would wait for.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- mbarrier
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

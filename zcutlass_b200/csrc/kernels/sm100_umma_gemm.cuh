@@ -169,6 +169,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // inputs/outputs may belong to the previous kernel on the stream
+  griddep_launch_dependents();
   const WaitCtx ctx{abort_flag, p.error_word};
 
   if (warp == 0) {

@@ -108,6 +108,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync_all();  // barrier inits and TMEM allocation visible to the peer
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // inputs/outputs may belong to the previous kernel on the stream
+  griddep_launch_dependents();
   const WaitCtx ctx{abort_flag, p.error_word};
   const int pair = blockIdx.x >> 1;
   const int npairs = gridDim.x >> 1;

@@ -3,6 +3,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "kernels/generic_gemm.cuh"
@@ -61,6 +62,26 @@ DeviceSlot* current_slot() {
   return slot;
 }
 
+// Programmatic stream serialization: a GEMM may be launched while the
+// previous kernel on its stream is still finishing, so its prologue (barrier
+// init, TMEM allocation, descriptor prefetch) and launch latency overlap that
+// kernel's tail; every kernel waits (griddepcontrol.wait) before its first
+// global memory access. ZCUTLASS_PDL=0 launches without it.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("ZCUTLASS_PDL");
+    return v == nullptr || v[0] != '0';
+  }();
+  return on;
+}
+
+void add_pdl_attr(cudaLaunchAttribute* attrs, unsigned int& n) {
+  if (!pdl_enabled()) return;
+  attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[n].val.programmaticStreamSerializationAllowed = 1;
+  ++n;
+}
+
 // Sets the dynamic shared memory limit of `kernel` once per device.
 template <typename Kernel>
 cudaError_t ensure_smem_attr(DeviceSlot* slot, int config_bit, Kernel kernel, int bytes) {
@@ -106,8 +127,19 @@ cudaError_t launch_umma_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit)
   cudaError_t e = ensure_smem_attr(slot, config_bit, kernel, L::kDynamicBytes);
   if (e != cudaSuccess) return e;
   const int grid = std::min(p.total_tiles, slot->info.sm_count);
-  kernel<<<grid, umma::kThreads, L::kDynamicBytes, a.stream>>>(ta, tb, td, p);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(umma::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = L::kDynamicBytes;
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr[1];
+  unsigned int nattr = 0;
+  add_pdl_attr(attr, nattr);
+  cfg.attrs = attr;
+  cfg.numAttrs = nattr;
+  e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, td, p);
   g_launches.fetch_add(1, std::memory_order_relaxed);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -151,13 +183,15 @@ cudaError_t launch_swapab_t(const LaunchArgs& a, DeviceSlot* slot, int config_bi
   cfg.blockDim = dim3(swapab::kThreads, 1, 1);
   cfg.dynamicSmemBytes = L::kDynamicBytes;
   cfg.stream = a.stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  unsigned int nattr = 1;
+  add_pdl_attr(attr, nattr);
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = nattr;
   e = cudaLaunchKernelEx(&cfg, kernel, tw, tx, p);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   if (e != cudaSuccess) return e;
@@ -204,13 +238,13 @@ cudaError_t launch_umma2_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit
   cfg.blockDim = dim3(umma2::kThreads, 1, 1);
   cfg.dynamicSmemBytes = L::kDynamicBytes;
   cfg.stream = a.stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 1;  // the occupancy query below sees the cluster shape only
   // Persistent grid: as many CTA pairs as can be resident at once (queried
   // once per device), never more than there are tiles.
   int& max_pairs = slot->max_active_pairs[config_bit];
@@ -222,6 +256,9 @@ cudaError_t launch_umma2_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit
     max_pairs = clusters;
   }
   cfg.gridDim = dim3(static_cast<unsigned>(2 * std::min(p.total_tiles, max_pairs)), 1, 1);
+  unsigned int nattr = 1;
+  add_pdl_attr(attr, nattr);
+  cfg.numAttrs = nattr;
   e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, td, p);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   if (e != cudaSuccess) return e;
@@ -305,8 +342,19 @@ cudaError_t launch_swapab_sk_t(const LaunchArgs& a, DeviceSlot* slot, int config
   auto kernel = swapab_sk::gemm_kernel<T, MP, STAGES, kDecodeKsub, KM>;
   e = ensure_smem_attr(slot, config_bit, kernel, L::kDynamicBytes);
   if (e != cudaSuccess) return e;
-  kernel<<<p.grid, swapab_sk::kThreads, L::kDynamicBytes, a.stream>>>(tw, tx, p);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.grid), 1, 1);
+  cfg.blockDim = dim3(swapab_sk::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = L::kDynamicBytes;
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr[1];
+  unsigned int nattr = 0;
+  add_pdl_attr(attr, nattr);
+  cfg.attrs = attr;
+  cfg.numAttrs = nattr;
+  e = cudaLaunchKernelEx(&cfg, kernel, tw, tx, p);
   g_launches.fetch_add(1, std::memory_order_relaxed);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -319,8 +367,19 @@ cudaError_t launch_generic_t(const LaunchArgs& a) {
   const int64_t tiles_m = (a.m + generic::kTile - 1) / generic::kTile;
   if (tiles_n > 2147483647LL) return cudaErrorInvalidValue;
   const dim3 grid(static_cast<unsigned>(tiles_n), static_cast<unsigned>(std::min<int64_t>(tiles_m, 65535)));
-  generic::gemm_kernel<T><<<grid, generic::kThreads, 0, a.stream>>>(p);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(generic::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr[1];
+  unsigned int nattr = 0;
+  add_pdl_attr(attr, nattr);
+  cfg.attrs = attr;
+  cfg.numAttrs = nattr;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, generic::gemm_kernel<T>, p);
   g_launches.fetch_add(1, std::memory_order_relaxed);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
