@@ -84,7 +84,8 @@ FAMILY_SHAPES = {
     "sk16": [(1, 128, 8192), (7, 300, 200), (16, 1000, 4096), (13, 7168, 1032), (16, 8192, 1024)],
     "sk32": [(17, 128, 128), (32, 520, 777), (25, 2048, 8192)],
     "sk64": [(33, 256, 256), (64, 1000, 1000), (48, 4096, 1536)],
-    "generic": [(5, 7, 9), (100, 200, 50), (130, 70, 300)],
+    # odd leading dimensions (pads 3/5/7/11) on several 128 x 128 tiles, K tails of 1..31
+    "generic": [(5, 7, 9), (100, 200, 50), (130, 70, 300), (1000, 777, 1032), (257, 1300, 2101)],
 }
 
 EPILOGUES = [  # (alpha, beta, bias)

@@ -138,7 +138,7 @@ class Sm100Operation final : public GemmOperation {
     desc_.a_type = desc_.b_type = desc_.c_type = desc_.d_type = type;
     desc_.accum_type = DType::F32;
     desc_.min_arch = kind == Kind::Generic ? arch::ArchKind::Sm80 : arch::ArchKind::Sm100;
-    desc_.op_class = kind == Kind::Generic ? arch::OpClass::Simt : arch::OpClass::Tcgen05;
+    desc_.op_class = kind == Kind::Generic ? arch::OpClass::TensorOp : arch::OpClass::Tcgen05;
     desc_.tile_m = tile_m;
     desc_.tile_n = tile_n;
     desc_.tile_k = tile_k;
@@ -271,8 +271,8 @@ void register_builtin_operations() {
       {"zcutlass_sm100_tcgen05_f16_128x256x64_ws_persistent", DType::F16, K::UmmaPersistent, 128, 256, 64, 4, F::Large, E::TmemRegisterTma},
       {"zcutlass_sm100_tcgen05_bf16_128x128x64_ws_persistent", DType::BF16, K::UmmaPersistent, 128, 128, 64, 6, F::Prefill, E::TmemRegisterTma},
       {"zcutlass_sm100_tcgen05_f16_128x128x64_ws_persistent", DType::F16, K::UmmaPersistent, 128, 128, 64, 6, F::Prefill, E::TmemRegisterTma},
-      {"zcutlass_sm100_simt_bf16_64x64x16_generic", DType::BF16, K::Generic, 64, 64, 16, 1, F::Fallback, E::RegisterLinear},
-      {"zcutlass_sm100_simt_f16_64x64x16_generic", DType::F16, K::Generic, 64, 64, 16, 1, F::Fallback, E::RegisterLinear},
+      {"zcutlass_sm100_mma_bf16_128x128x32_generic", DType::BF16, K::Generic, 128, 128, 32, 2, F::Fallback, E::RegisterLinear},
+      {"zcutlass_sm100_mma_f16_128x128x32_generic", DType::F16, K::Generic, 128, 128, 32, 2, F::Fallback, E::RegisterLinear},
   };
   auto& manifest = gemm_api::global_manifest();
   for (const auto& op : ops) manifest.append(&op);

@@ -363,8 +363,8 @@ cudaError_t launch_generic_t(const LaunchArgs& a) {
   GenericGemmParams p{a.m,   a.n,   a.k,   a.a,     a.lda,  a.b,   a.ldb,
                       a.c,   a.ldc, a.d,   a.ldd,   a.bias, a.alpha, a.beta,
                       a.b_col_major ? 1 : 0};
-  const int64_t tiles_n = (a.n + generic::kTile - 1) / generic::kTile;
-  const int64_t tiles_m = (a.m + generic::kTile - 1) / generic::kTile;
+  const int64_t tiles_n = (a.n + generic::kTileN - 1) / generic::kTileN;
+  const int64_t tiles_m = (a.m + generic::kTileM - 1) / generic::kTileM;
   if (tiles_n > 2147483647LL) return cudaErrorInvalidValue;
   const dim3 grid(static_cast<unsigned>(tiles_n), static_cast<unsigned>(std::min<int64_t>(tiles_m, 65535)));
   cudaLaunchConfig_t cfg{};
