@@ -228,3 +228,32 @@ def test_streamk_in_cuda_graph_replays(cuda_device, monkeypatch):
             torch.cuda.synchronize()
             assert torch.equal(d, ref) and torch.equal(d2, ref2)
     assert _native.device_error(clear=True) == 0
+
+
+@pytest.mark.gpu
+def test_streamk_capture_on_fresh_stream_falls_back(cuda_device, monkeypatch):
+    """With the experimental stream-K kernel enabled, a decode GEMM captured on
+    a stream that has no stream-K workspace yet (its allocation is not allowed
+    during capture) is served by split-K instead of failing the capture."""
+    import torch
+
+    monkeypatch.setenv("ZCUTLASS_EXPERIMENTAL_KERNELS", "1")
+    m, n, k = 8, 1280, 8192
+    g0 = torch.Generator(device="cpu").manual_seed(5)
+    a = torch.randn(m, k, generator=g0).to(torch.bfloat16).cuda()
+    w = (torch.randn(n, k, generator=g0) / k ** 0.5).to(torch.bfloat16).cuda()
+    s = torch.cuda.Stream()
+    desc = _native.make_desc(m, n, k, k, k, n, n, BF16, stream=s.cuda_stream, b_layout=_native.COLUMN_MAJOR)
+    assert "swapab_streamk" in _native.selected_kernel(desc)["kernel_name"]  # outside capture
+    d = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        desc.stream = torch.cuda.current_stream().cuda_stream
+        assert _native.gemm(desc, a.data_ptr(), w.data_ptr(), None, d.data_ptr()) == 0
+    d.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    ref = torch.nn.functional.linear(a.float(), w.float())
+    rel = float((d.float() - ref).norm() / ref.norm())
+    assert rel < 5e-3, rel
+    assert _native.device_error(clear=True) == 0

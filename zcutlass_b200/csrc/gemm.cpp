@@ -178,6 +178,10 @@ class Sm100Operation final : public GemmOperation {
     if (kind_ == Kind::UmmaSwapAb || kind_ == Kind::UmmaSwapAbStreamK) {
       const int mp = desc_.tile_m;
       if (m > mp) return false;
+      // The stream-K workspace is allocated on a stream's first use, which a
+      // CUDA graph capture forbids: while capturing, only a stream whose
+      // workspace already fits qualifies (split-K takes the call otherwise).
+      if (kind_ == Kind::UmmaSwapAbStreamK && !zcb::swapab_sk_ready_for_stream(m, n, k, args.stream)) return false;
       if (forced) return true;
       if (mp > 16 && m <= mp / 2) return false;
       if (n < 128 || k < 128) return false;

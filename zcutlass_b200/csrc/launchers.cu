@@ -306,6 +306,17 @@ cudaError_t acquire_workspace(int dev, cudaStream_t stream, size_t counter_need,
   return cudaSuccess;
 }
 
+// Workspace bytes the stream-K kernel needs for (m, n, k): tile counters and
+// two partial slots per CTA (MP = m rounded up to 16, 32 or 64).
+void swapab_sk_needs(int64_t m, int64_t n, int64_t k, int sm_count, size_t* counter_need, size_t* partial_need) {
+  const int mp = m <= 16 ? 16 : (m <= 32 ? 32 : 64);
+  const int64_t tiles_n = (n + swapab_sk::kBlockN - 1) / swapab_sk::kBlockN;
+  const int64_t num_kb = (k + kDecodeKBlock - 1) / kDecodeKBlock;
+  const int64_t grid = std::min<int64_t>(tiles_n * num_kb, sm_count);
+  *counter_need = size_t(tiles_n) * 8;
+  *partial_need = size_t(2) * grid * mp * swapab_sk::kBlockN * sizeof(float);
+}
+
 template <typename T, int MP, int STAGES, bool KM>
 cudaError_t launch_swapab_sk_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit) {
   using L = swapab_sk::Smem<MP, STAGES, kDecodeKsub>;
@@ -516,6 +527,22 @@ cudaError_t launch_umma_swapab_sk_gemm(const LaunchArgs& a) {
   DeviceSlot* slot = current_slot();
   if (slot == nullptr) return cudaErrorInvalidDevice;
   return a.b_col_major ? launch_swapab_sk_km<true>(a, slot) : launch_swapab_sk_km<false>(a, slot);
+}
+
+bool swapab_sk_ready_for_stream(int64_t m, int64_t n, int64_t k, cudaStream_t stream) {
+  cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &status) != cudaSuccess) {
+    (void)cudaGetLastError();  // no device (host-only telemetry): not capturing
+    return true;
+  }
+  if (status == cudaStreamCaptureStatusNone) return true;
+  DeviceSlot* slot = current_slot();
+  if (slot == nullptr) return false;
+  size_t counter_need = 0, partial_need = 0;
+  swapab_sk_needs(m, n, k, slot->info.sm_count, &counter_need, &partial_need);
+  std::lock_guard<std::mutex> lock(g_ws_mutex);
+  const auto it = g_ws.find({slot->info.ordinal, stream});
+  return it != g_ws.end() && it->second.counter_bytes >= counter_need && it->second.partial_bytes >= partial_need;
 }
 
 bool swapab_prefer_streamk(int64_t n, int64_t k, int sm_count) {

@@ -47,6 +47,10 @@ cudaError_t launch_umma_swapab_gemm(const LaunchArgs& args, int* splits_used);
 // workspace owned by the library.
 cudaError_t launch_umma_swapab_sk_gemm(const LaunchArgs& args);
 bool swapab_prefer_streamk(int64_t n, int64_t k, int sm_count);
+// False only while `stream` is being captured into a CUDA graph and its
+// stream-K workspace does not yet fit an (m, n, k) problem (a first-use
+// allocation is not allowed during capture).
+bool swapab_sk_ready_for_stream(int64_t m, int64_t n, int64_t k, cudaStream_t stream);
 // Predicated CUDA-core kernel for TMA-incompatible layouts.
 cudaError_t launch_generic_gemm(const LaunchArgs& args);
 
