@@ -223,12 +223,16 @@ def decode_sweep(device, peaks: dict, iters: int = 200) -> list[dict]:
                 return [_native.make_desc(m, n, k, k, k, n, n, _native.BF16, stream=stream,
                                           b_layout=_native.COLUMN_MAJOR) for _ in ws]
 
-            eager = make_descs()
-            for i in range(2 * copies):
-                run(i, eager)
+            # warm-up and capture on one stream, so per-stream state (the
+            # experimental stream-K workspace) exists before the capture
+            side = torch.cuda.Stream(device)
+            with torch.cuda.stream(side):
+                eager = make_descs()
+                for i in range(2 * copies):
+                    run(i, eager)
             torch.cuda.synchronize()
             graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+            with torch.cuda.graph(graph, stream=side, capture_error_mode="thread_local"):
                 captured = make_descs()
                 for i in range(iters):
                     run(i, captured)
