@@ -38,6 +38,7 @@ namespace swapab {
 constexpr int kBlockN = 128;  // rows of D^T per CTA (MMA M)
 constexpr int kBlockK = 64;   // one 128-byte swizzle row of K; a stage holds KSUB of them
 constexpr int kThreads = 192;
+constexpr int kMaxSplits = 8;  // cluster size limit (portable)
 
 // A pipeline stage holds KSUB K sub-blocks of 64: TMA streams a weight
 // matrix at ~4.7 TB/s with 16 KiB per stage but ~5.7 TB/s with >= 32 KiB
@@ -250,8 +251,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n = n0 + rl;
       if (n >= p.n) continue;
       const uint32_t off = static_cast<uint32_t>((mi * kBlockN + rl) * 4);
-      float sum = 0.0f;
-      for (int s = 0; s < p.splits; ++s) sum += ld_dsmem_f32(red_addr + off, static_cast<uint32_t>(s));
+      // all of an element's remote loads first (one DSMEM round trip, not S)
+      float part[kMaxSplits];
+#pragma unroll
+      for (int s = 0; s < kMaxSplits; ++s)
+        part[s] = s < p.splits ? ld_dsmem_f32(red_addr + off, static_cast<uint32_t>(s)) : 0.0f;
+      float sum = 0.0f;  // in split order, as before: the result does not depend on timing
+#pragma unroll
+      for (int s = 0; s < kMaxSplits; ++s)
+        if (s < p.splits) sum += part[s];
       float v = p.alpha * sum;
       if (has_c) v += p.beta * Elem<T>::to_float(cptr[static_cast<int64_t>(mi) * p.ldc + n]);
       if (has_bias) v += Elem<T>::to_float(bptr[n]);
