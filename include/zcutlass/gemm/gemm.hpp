@@ -87,6 +87,18 @@ struct GemmDesc {
 Status gemm(const GemmDesc& desc, const void* A, const void* B, const void* C, void* D);
 
 Status gemm(const gemm_api::GemmArguments& args);
+
+// Addition without a reference counterpart: the same GEMM with the rows of A
+// gathered from `parts` buffers (1..8), e.g. the row shards of a sequence-
+// parallel activation in peer-mapped memory of each tensor-parallel rank.
+// Rows [i * M / parts, (i + 1) * M / parts) are read from a_parts[i], which
+// points to a full [M, K] row-major matrix with leading dimension desc.lda
+// (only its own rows are read). B must be column-major (a [N, K] weight).
+// NotSupported unless M is a multiple of parts and every block of rows is a
+// multiple of 128 (of 256 where the 256 x 256 two-CTA tiles are chosen), and
+// every operand satisfies the tcgen05 kernels' alignment rules.
+Status gemm_gather_a(const GemmDesc& desc, const void* const* a_parts, int parts, const void* B, const void* C,
+                     void* D);
 // Argument validation only (same contract as the reference: no kernel selection).
 Status can_implement(const gemm_api::GemmArguments& args);
 // Always 0: no kernel in this library needs a caller-provided workspace.

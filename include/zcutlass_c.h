@@ -25,6 +25,9 @@
  *   zcutlass_selftest_bounded_wait runs a kernel whose bounded wait must expire
  *   zcutlass_gemm_decode_noalloc   decode GEMM that allocates nothing
  *   zcutlass_nvls_allreduce     row-parallel all-reduce over NVLink SHARP
+ *   zcutlass_nvls_reduce_scatter   reduce-scatter over NVLink SHARP
+ *   zcutlass_nvls_barrier       the collectives' cross-rank barrier alone
+ *   zcutlass_gemm_gather_a      GEMM reading row blocks of A from several buffers
  *
  * Integer enum values equal the C++ enum values (Status, DType, LayoutKind).
  * Return values of type int that carry a status use zcutlass_status values.
@@ -81,6 +84,13 @@ int zcutlass_gemm_rowmajor(int64_t m, int64_t n, int64_t k, const void* A, int64
                            const void* B, int64_t ldb, const void* C, int64_t ldc, void* D,
                            int64_t ldd, int32_t dtype, float alpha, float beta,
                            const void* bias, void* stream);
+
+/* zcutlass_gemm with the rows of A gathered from `parts` (1..8) buffers; no
+ * reference counterpart (see zcutlass::gemm_gather_a in
+ * include/zcutlass/gemm/gemm.hpp for the contract). Returns
+ * ZCUTLASS_NOT_SUPPORTED when the layout cannot be served by its kernels. */
+int zcutlass_gemm_gather_a(const zcutlass_gemm_desc* desc, const void* const* a_parts, int32_t parts,
+                           const void* B, const void* C, void* D);
 
 int zcutlass_can_implement(const zcutlass_gemm_desc* desc, const void* A, const void* B,
                            const void* C, const void* D);
@@ -162,6 +172,24 @@ int zcutlass_gemm_decode_noalloc(int64_t m, int64_t n, int64_t k, const void* A,
  * Asynchronous on `stream` (three kernel launches). */
 int zcutlass_nvls_allreduce(void* mc_ptr, int64_t nbytes, int32_t dtype, void* mc_flag, void* flag,
                             int32_t rank, int32_t world, void* stream);
+
+/* The cross-rank barrier of the two collectives on its own (no reference
+ * counterpart): same barrier words and contract. Every rank's earlier work on
+ * `stream` is complete and visible to all ranks when it returns on the
+ * stream (bounded wait: two seconds, then the device error word). */
+int zcutlass_nvls_barrier(void* mc_flag, void* flag, int32_t world, void* stream);
+
+/* Reduce-scatter over NVLink SHARP (no reference counterpart), for a
+ * sequence-parallel layer: same buffer, barrier and ordering contract as
+ * zcutlass_nvls_allreduce. `nbytes` (a multiple of 16 * world) is split into
+ * `world` equal contiguous slices; rank r sums slice r over all ranks (FP32
+ * accumulation in the switch) and stores it into its own copy, `local_ptr`
+ * being the local address of the data `mc_ptr` maps. The other slices of the
+ * local copy are left as they were. After the call returns on the stream,
+ * every rank's slice is final on that rank (the closing barrier), so peers
+ * may read it. */
+int zcutlass_nvls_reduce_scatter(void* mc_ptr, void* local_ptr, int64_t nbytes, int32_t dtype, void* mc_flag,
+                                 void* flag, int32_t rank, int32_t world, void* stream);
 
 /* Failure-detection self test (no reference counterpart): launches one kernel
  * whose bounded mbarrier wait is never satisfied, with a limit of `timeout_us`

@@ -171,3 +171,40 @@ def test_gemm_desc_layout_matches_c_header():
     assert names[:7] == ["m", "n", "k", "lda", "ldb", "ldc", "ldd"]
     assert names[7:11] == ["a_type", "b_type", "c_type", "d_type"]
     assert ctypes.sizeof(N.GemmDesc) == 7 * 8 + 4 * 4 + 2 * 4 + 2 * 8 + 4 * 4
+
+
+def test_gather_a_argument_checks():
+    """zcutlass_gemm_gather_a rejects bad part lists and layouts its kernels
+    cannot serve before launching anything (no GPU needed)."""
+    P = 1 << 20  # 16-byte aligned dummy addresses; nothing is dereferenced on these paths
+
+    def call(m, n, k, parts, *, col=True, ptrs=None):
+        desc = N.make_desc(m, n, k, k, k if col else n, n, n, N.BF16,
+                           b_layout=N.COLUMN_MAJOR if col else N.ROW_MAJOR)
+        ptrs = [P * (i + 1) for i in range(parts)] if ptrs is None else ptrs
+        arr = (ctypes.c_void_p * max(1, len(ptrs)))(*ptrs)
+        return N.lib().zcutlass_gemm_gather_a(ctypes.byref(desc), arr, parts, P * 16, None, P * 32)
+
+    assert call(1024, 1024, 1024, 0, ptrs=[P]) == N.INVALID_ARGUMENT
+    assert call(1024, 1024, 1024, 9) == N.INVALID_ARGUMENT
+    assert call(1024, 1024, 1024, 2, ptrs=[P, None]) == N.INVALID_ARGUMENT
+    assert call(1024, 1024, 1024, 4, col=False) == N.NOT_SUPPORTED      # B must be a [N, K] weight
+    assert call(1000, 1024, 1024, 8) == N.NOT_SUPPORTED                 # 125-row blocks split tiles
+    assert call(1024, 1024, 1024, 3) == N.NOT_SUPPORTED                 # M not a multiple of parts
+    assert call(0, 1024, 1024, 4) == N.SUCCESS                          # zero size: nothing to do
+    assert N.lib().zcutlass_gemm_gather_a(None, None, 1, None, None, None) == N.INVALID_ARGUMENT
+
+
+def test_nvls_collective_argument_checks():
+    lib = N.lib()
+    flag = 1 << 20
+    assert lib.zcutlass_nvls_reduce_scatter(None, flag, 4096, N.BF16, flag, flag, 0, 2, None) == N.INVALID_ARGUMENT
+    # 4096 + 16 bytes do not split into 2 slices of whole 16-byte words
+    assert lib.zcutlass_nvls_reduce_scatter(flag, flag, 4096 + 16, N.BF16, flag, flag, 0, 2, None) == \
+        N.INVALID_ARGUMENT
+    assert lib.zcutlass_nvls_reduce_scatter(flag, flag, 4096, N.BF16, flag, flag, 2, 2, None) == \
+        N.INVALID_ARGUMENT  # rank out of range
+    assert lib.zcutlass_nvls_reduce_scatter(flag, flag, 4096, N.F32, flag, flag, 0, 2, None) == N.NOT_SUPPORTED
+    assert lib.zcutlass_nvls_allreduce(flag, 4096, N.BF16, flag, flag + 4, 0, 2, None) == \
+        N.INVALID_ARGUMENT  # barrier words must be 8-byte aligned
+    assert lib.zcutlass_nvls_barrier(None, flag, 2, None) == N.INVALID_ARGUMENT

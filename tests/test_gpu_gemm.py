@@ -12,7 +12,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from gemm_case import Case, check_case, make_inputs, oracle_result, run_zcutlass, selected
+from gemm_case import Case, check_case, make_inputs, oracle_result, run_zcutlass, selected, to_device, to_host
 from oracle import oracle
 from zcutlass_b200 import _native
 
@@ -257,3 +257,43 @@ def test_streamk_capture_on_fresh_stream_falls_back(cuda_device, monkeypatch):
     rel = float((d.float() - ref).norm() / ref.norm())
     assert rel < 5e-3, rel
     assert _native.device_error(clear=True) == 0
+
+
+# ---------------------------------------------------------------- row-gathered A
+
+GATHER_CASES = [  # (m, n, k, parts, alpha, beta, bias)
+    (256, 2048, 512, 2, 1.0, 0.0, False),     # 128-row blocks: one-CTA kernel
+    (1024, 1536, 520, 4, 0.75, 0.5, True),    # ragged K, epilogue with C and bias
+    (2048, 4096, 1024, 8, 1.0, 0.0, False),   # 256-row blocks: two-CTA tiles
+    (4096, 3584, 1024, 8, 1.0, 0.0, True),    # TP8 gate_up shard width at 4096 tokens
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,n,k,parts,alpha,beta,bias", GATHER_CASES)
+def test_gemm_gather_a(cuda_device, m, n, k, parts, alpha, beta, bias):
+    """zcutlass_gemm_gather_a reads row block i of A from buffer i only: every
+    buffer holds a full [M, K] matrix whose other rows are garbage."""
+    import torch
+
+    c = Case(f"gather {m}x{n}x{k}/{parts}", BF16, m, n, k, alpha, beta, bias, b_col_major=True, gen="normal",
+             seed=parts)
+    a, b, cm, bias_bits = make_inputs(c)
+    ref = oracle_result(c, a, b, cm, bias_bits)
+    rows = m // parts
+    bufs = []
+    for i in range(parts):
+        junk = np.full_like(a, oracle.float_to_bits(np.float32(1000.0 + i), BF16))
+        junk[i * rows:(i + 1) * rows] = a[i * rows:(i + 1) * rows]
+        bufs.append(to_device(junk))
+    db, dc, dbias = to_device(b), to_device(cm), to_device(bias_bits)
+    dd = torch.empty(m, n, device="cuda", dtype=torch.int16)
+    desc = _native.make_desc(m, n, k, k, k, n, n, BF16, alpha, beta, dbias.data_ptr() if bias else None, None,
+                             b_layout=_native.COLUMN_MAJOR)
+    st = _native.gemm_gather_a(desc, [t.data_ptr() for t in bufs], db.data_ptr(),
+                               dc.data_ptr() if beta != 0.0 else None, dd.data_ptr())
+    torch.cuda.synchronize()
+    assert st == _native.SUCCESS, _native.STATUS_NAMES.get(st, st)
+    assert _native.device_error(clear=True) == 0
+    out = oracle.bits_to_float(to_host(dd), BF16)
+    oracle.check(out, ref, BF16)

@@ -69,6 +69,7 @@ SIGNATURES = {
     "zcutlass_gemm_rowmajor": (ctypes.c_int, [_i64, _i64, _i64, _v, _i64, _v, _i64, _v, _i64, _v, _i64,
                                               ctypes.c_int32, ctypes.c_float, ctypes.c_float, _v, _v]),
     "zcutlass_can_implement": (ctypes.c_int, [_P, _v, _v, _v, _v]),
+    "zcutlass_gemm_gather_a": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32, _v, _v, _v]),
     "zcutlass_get_workspace_size": (ctypes.c_size_t, [_P]),
     "zcutlass_selected_kernel_name": (ctypes.c_char_p, [_P]),
     "zcutlass_selected_kernel_family": (ctypes.c_char_p, [_P]),
@@ -90,6 +91,9 @@ SIGNATURES = {
     "zcutlass_selftest_bounded_wait": (ctypes.c_int, [ctypes.c_uint32]),
     "zcutlass_nvls_allreduce": (ctypes.c_int, [_v, _i64, ctypes.c_int32, _v, _v, ctypes.c_int32, ctypes.c_int32,
                                                _v]),
+    "zcutlass_nvls_barrier": (ctypes.c_int, [_v, _v, ctypes.c_int32, _v]),
+    "zcutlass_nvls_reduce_scatter": (ctypes.c_int, [_v, _v, _i64, ctypes.c_int32, _v, _v, ctypes.c_int32,
+                                                    ctypes.c_int32, _v]),
     "zcutlass_gemm_decode_noalloc": (ctypes.c_int, [_i64, _i64, _i64, _v, _i64, _v, _i64, ctypes.c_int32, _v, _i64,
                                                     _v, _i64, ctypes.c_int32, ctypes.c_float, ctypes.c_float, _v,
                                                     _v]),
@@ -127,6 +131,12 @@ def gemm_rowmajor(m, n, k, a, lda, b, ldb, c, ldc, d, ldd, dtype, alpha=1.0, bet
                   stream=None) -> int:
     return lib().zcutlass_gemm_rowmajor(m, n, k, a, lda, b, ldb, c, ldc, d, ldd, dtype, alpha, beta,
                                         bias, stream)
+
+
+def gemm_gather_a(desc: GemmDesc, a_parts, b, c, d) -> int:
+    """zcutlass_gemm_gather_a: rows of A in len(a_parts) row blocks, block i read from a_parts[i]."""
+    arr = (ctypes.c_void_p * max(1, len(a_parts)))(*a_parts)
+    return lib().zcutlass_gemm_gather_a(ctypes.byref(desc), arr, len(a_parts), b, c, d)
 
 
 def can_implement(desc: GemmDesc, a, b, c, d) -> int:

@@ -51,6 +51,12 @@ int zcutlass_gemm_rowmajor(int64_t m, int64_t n, int64_t k, const void* A, int64
   return static_cast<int>(zcutlass::gemm(g, A, B, C, D));
 }
 
+int zcutlass_gemm_gather_a(const zcutlass_gemm_desc* desc, const void* const* a_parts, int32_t parts,
+                           const void* B, const void* C, void* D) {
+  if (desc == nullptr) return ZCUTLASS_INVALID_ARGUMENT;
+  return static_cast<int>(zcutlass::gemm_gather_a(to_desc(desc), a_parts, parts, B, C, D));
+}
+
 int zcutlass_can_implement(const zcutlass_gemm_desc* desc, const void* A, const void* B,
                            const void* C, const void* D) {
   if (desc == nullptr) return ZCUTLASS_INVALID_ARGUMENT;
@@ -123,6 +129,23 @@ int zcutlass_nvls_allreduce(void* mc_ptr, int64_t nbytes, int32_t dtype, void* m
   const cudaError_t e = zcb::launch_nvls_allreduce(mc_ptr, nbytes, dtype == ZCUTLASS_BF16,
                                                    static_cast<uint32_t*>(mc_flag), static_cast<uint32_t*>(flag), rank,
                                                    world, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ZCUTLASS_SUCCESS
+                          : (e == cudaErrorInvalidValue ? ZCUTLASS_INVALID_ARGUMENT : ZCUTLASS_RUNTIME_ERROR);
+}
+
+int zcutlass_nvls_barrier(void* mc_flag, void* flag, int32_t world, void* stream) {
+  const cudaError_t e = zcb::launch_nvls_barrier(static_cast<uint32_t*>(mc_flag), static_cast<uint32_t*>(flag), world,
+                                                 static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ZCUTLASS_SUCCESS
+                          : (e == cudaErrorInvalidValue ? ZCUTLASS_INVALID_ARGUMENT : ZCUTLASS_RUNTIME_ERROR);
+}
+
+int zcutlass_nvls_reduce_scatter(void* mc_ptr, void* local_ptr, int64_t nbytes, int32_t dtype, void* mc_flag,
+                                 void* flag, int32_t rank, int32_t world, void* stream) {
+  if (dtype != ZCUTLASS_F16 && dtype != ZCUTLASS_BF16) return ZCUTLASS_NOT_SUPPORTED;
+  const cudaError_t e = zcb::launch_nvls_reduce_scatter(mc_ptr, local_ptr, nbytes, dtype == ZCUTLASS_BF16,
+                                                        static_cast<uint32_t*>(mc_flag), static_cast<uint32_t*>(flag),
+                                                        rank, world, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? ZCUTLASS_SUCCESS
                           : (e == cudaErrorInvalidValue ? ZCUTLASS_INVALID_ARGUMENT : ZCUTLASS_RUNTIME_ERROR);
 }

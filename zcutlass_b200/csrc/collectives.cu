@@ -96,12 +96,13 @@ constexpr int kArThreads = 256;
 constexpr int kArUnroll = 4;
 constexpr int kArMaxBlocks = 32;
 
-template <bool kBf16>
-__global__ void __launch_bounds__(kArThreads) nvls_allreduce_kernel(uint8_t* mc, int64_t words16, int rank,
-                                                                    int world) {
-  const int64_t lo = words16 * rank / world;
-  const int64_t n = words16 * (rank + 1) / world - lo;
+// Reduces 16-byte words [lo, lo + n) across all ranks. kBroadcast: the sums go
+// back to every rank's copy (all-reduce); otherwise only to this rank's copy
+// at `local` (reduce-scatter).
+template <bool kBf16, bool kBroadcast>
+__global__ void __launch_bounds__(kArThreads) nvls_reduce_kernel(uint8_t* mc, uint8_t* local, int64_t lo, int64_t n) {
   uint8_t* base = mc + lo * 16;
+  uint8_t* dst = local + lo * 16;
   const int64_t step = static_cast<int64_t>(gridDim.x) * kArThreads * kArUnroll;
   for (int64_t j = static_cast<int64_t>(blockIdx.x) * kArThreads * kArUnroll + threadIdx.x; j < n; j += step) {
     uint4 v[kArUnroll];
@@ -113,7 +114,13 @@ __global__ void __launch_bounds__(kArThreads) nvls_allreduce_kernel(uint8_t* mc,
 #pragma unroll
     for (int u = 0; u < kArUnroll; ++u) {
       const int64_t idx = j + static_cast<int64_t>(u) * kArThreads;
-      if (idx < n) multimem_st<kBf16>(base + idx * 16, v[u]);
+      if (idx < n) {
+        if constexpr (kBroadcast) {
+          multimem_st<kBf16>(base + idx * 16, v[u]);
+        } else {
+          *reinterpret_cast<uint4*>(dst + idx * 16) = v[u];
+        }
+      }
     }
   }
 }
@@ -131,8 +138,10 @@ cudaError_t ensure_carveout(int device) {
   std::call_once(g_carveout_once[device], [&result] {
     const int carve = cudaSharedmemCarveoutMaxShared;
     for (const void* k : {reinterpret_cast<const void*>(&nvls_barrier_kernel),
-                          reinterpret_cast<const void*>(&nvls_allreduce_kernel<true>),
-                          reinterpret_cast<const void*>(&nvls_allreduce_kernel<false>)}) {
+                          reinterpret_cast<const void*>(&nvls_reduce_kernel<true, true>),
+                          reinterpret_cast<const void*>(&nvls_reduce_kernel<false, true>),
+                          reinterpret_cast<const void*>(&nvls_reduce_kernel<true, false>),
+                          reinterpret_cast<const void*>(&nvls_reduce_kernel<false, false>)}) {
       const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, carve);
       if (e != cudaSuccess && result == cudaSuccess) result = e;
     }
@@ -142,34 +151,76 @@ cudaError_t ensure_carveout(int device) {
 
 }  // namespace
 
+namespace {
+
+// barrier -> reduce words [lo, lo + n) -> barrier, all on `stream`.
+cudaError_t launch_reduce(void* mc_ptr, void* local_ptr, int64_t lo, int64_t n, bool bf16, bool broadcast,
+                          uint32_t* mc_flag, uint32_t* flag, int world, cudaStream_t stream) {
+  const DeviceInfo* info = current_device_info();
+  if (info == nullptr) return cudaErrorInvalidDevice;
+  const cudaError_t ce = ensure_carveout(info->ordinal);
+  if (ce != cudaSuccess) return ce;
+  const int64_t per_block = static_cast<int64_t>(kArThreads) * kArUnroll;
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((n + per_block - 1) / per_block, kArMaxBlocks));
+  const uint32_t w = static_cast<uint32_t>(world);
+  auto* mc = static_cast<uint8_t*>(mc_ptr);
+  auto* local = static_cast<uint8_t*>(local_ptr);
+  const dim3 grid(static_cast<unsigned>(blocks));
+
+  nvls_barrier_kernel<<<1, 32, 0, stream>>>(mc_flag, flag, w, kWaitTimeoutNs, kErrNvlsBarrierPre, info->error_word);
+  if (broadcast) {
+    if (bf16) nvls_reduce_kernel<true, true><<<grid, kArThreads, 0, stream>>>(mc, local, lo, n);
+    else nvls_reduce_kernel<false, true><<<grid, kArThreads, 0, stream>>>(mc, local, lo, n);
+  } else {
+    if (bf16) nvls_reduce_kernel<true, false><<<grid, kArThreads, 0, stream>>>(mc, local, lo, n);
+    else nvls_reduce_kernel<false, false><<<grid, kArThreads, 0, stream>>>(mc, local, lo, n);
+  }
+  nvls_barrier_kernel<<<1, 32, 0, stream>>>(mc_flag, flag, w, kWaitTimeoutNs, kErrNvlsBarrierPost, info->error_word);
+  count_launches(3);
+  return cudaGetLastError();
+}
+
+bool common_args_ok(const void* mc_ptr, int64_t nbytes, const uint32_t* mc_flag, const uint32_t* flag, int rank,
+                    int world) {
+  return mc_ptr != nullptr && nbytes > 0 && (nbytes & 15) == 0 && (reinterpret_cast<uintptr_t>(mc_ptr) & 15) == 0 &&
+         mc_flag != nullptr && flag != nullptr && (reinterpret_cast<uintptr_t>(mc_flag) & 3) == 0 &&
+         (reinterpret_cast<uintptr_t>(flag) & 7) == 0 && world >= 1 && rank >= 0 && rank < world;
+}
+
+}  // namespace
+
 cudaError_t launch_nvls_allreduce(void* mc_ptr, int64_t nbytes, bool bf16, uint32_t* mc_flag, uint32_t* flag,
                                   int rank, int world, cudaStream_t stream) {
-  if (mc_ptr == nullptr || nbytes <= 0 || (nbytes & 15) != 0 || (reinterpret_cast<uintptr_t>(mc_ptr) & 15) != 0 ||
-      mc_flag == nullptr || flag == nullptr || (reinterpret_cast<uintptr_t>(mc_flag) & 3) != 0 ||
-      (reinterpret_cast<uintptr_t>(flag) & 7) != 0 || world < 1 || rank < 0 || rank >= world) {
+  if (!common_args_ok(mc_ptr, nbytes, mc_flag, flag, rank, world)) return cudaErrorInvalidValue;
+  const int64_t words = nbytes / 16;
+  const int64_t lo = words * rank / world;
+  const int64_t n = words * (rank + 1) / world - lo;
+  return launch_reduce(mc_ptr, mc_ptr, lo, n, bf16, true, mc_flag, flag, world, stream);
+}
+
+cudaError_t launch_nvls_barrier(uint32_t* mc_flag, uint32_t* flag, int world, cudaStream_t stream) {
+  if (mc_flag == nullptr || flag == nullptr || (reinterpret_cast<uintptr_t>(mc_flag) & 3) != 0 ||
+      (reinterpret_cast<uintptr_t>(flag) & 7) != 0 || world < 1) {
     return cudaErrorInvalidValue;
   }
   const DeviceInfo* info = current_device_info();
   if (info == nullptr) return cudaErrorInvalidDevice;
   const cudaError_t ce = ensure_carveout(info->ordinal);
   if (ce != cudaSuccess) return ce;
-  const int64_t words = nbytes / 16;
-  const int64_t per_rank = (words + world - 1) / world;
-  const int64_t per_block = static_cast<int64_t>(kArThreads) * kArUnroll;
-  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((per_rank + per_block - 1) / per_block, kArMaxBlocks));
-  const uint32_t w = static_cast<uint32_t>(world);
-
-  nvls_barrier_kernel<<<1, 32, 0, stream>>>(mc_flag, flag, w, kWaitTimeoutNs, kErrNvlsBarrierPre, info->error_word);
-  if (bf16) {
-    nvls_allreduce_kernel<true><<<static_cast<unsigned>(blocks), kArThreads, 0, stream>>>(
-        static_cast<uint8_t*>(mc_ptr), words, rank, world);
-  } else {
-    nvls_allreduce_kernel<false><<<static_cast<unsigned>(blocks), kArThreads, 0, stream>>>(
-        static_cast<uint8_t*>(mc_ptr), words, rank, world);
-  }
-  nvls_barrier_kernel<<<1, 32, 0, stream>>>(mc_flag, flag, w, kWaitTimeoutNs, kErrNvlsBarrierPost, info->error_word);
-  count_launches(3);
+  nvls_barrier_kernel<<<1, 32, 0, stream>>>(mc_flag, flag, static_cast<uint32_t>(world), kWaitTimeoutNs,
+                                             kErrNvlsBarrierPre, info->error_word);
+  count_launches(1);
   return cudaGetLastError();
+}
+
+cudaError_t launch_nvls_reduce_scatter(void* mc_ptr, void* local_ptr, int64_t nbytes, bool bf16, uint32_t* mc_flag,
+                                       uint32_t* flag, int rank, int world, cudaStream_t stream) {
+  if (!common_args_ok(mc_ptr, nbytes, mc_flag, flag, rank, world) || local_ptr == nullptr ||
+      (reinterpret_cast<uintptr_t>(local_ptr) & 15) != 0 || nbytes % (16 * static_cast<int64_t>(world)) != 0) {
+    return cudaErrorInvalidValue;
+  }
+  const int64_t n = nbytes / 16 / world;  // equal contiguous slices, one per rank
+  return launch_reduce(mc_ptr, local_ptr, n * rank, n, bf16, false, mc_flag, flag, world, stream);
 }
 
 }  // namespace zcb

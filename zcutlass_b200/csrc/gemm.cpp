@@ -316,6 +316,57 @@ Status gemm(const GemmDesc& desc, const void* A, const void* B, const void* C, v
   return op->run(args, {});
 }
 
+Status gemm_gather_a(const GemmDesc& desc, const void* const* a_parts, int parts, const void* B, const void* C,
+                     void* D) {
+  if (a_parts == nullptr || parts < 1 || parts > zcb::kMaxAParts) return Status::InvalidArgument;
+  const Status validation = validate_desc(desc, a_parts[0], B, C, D);
+  if (validation != Status::Success) return validation;
+  if (desc.m == 0 || desc.n == 0 || desc.k == 0) return Status::Success;
+  for (int i = 0; i < parts; ++i)
+    if (a_parts[i] == nullptr) return Status::InvalidArgument;
+  // Served by the persistent tcgen05 kernels only: TMA-describable operands,
+  // a [N, K] weight, and row blocks that never split a tile.
+  if (desc.b_layout != layout::LayoutKind::ColumnMajor) return Status::NotSupported;
+  const SelectDevice dev = select_device();
+  if (dev.cc_major != 10 || dev.cc_minor != 0) return Status::NotSupported;
+  if (desc.m > INT_MAX || desc.n > INT_MAX || desc.k > INT_MAX || desc.m % parts != 0) return Status::NotSupported;
+  for (int i = 0; i < parts; ++i)
+    if (!zcb::tma_compatible(a_parts[i], desc.lda)) return Status::NotSupported;
+  if (!zcb::tma_compatible(B, desc.ldb) || !zcb::tma_compatible(D, desc.ldd)) return Status::NotSupported;
+  if (desc.beta != 0.0f && (!aligned16(C) || (desc.ldc & 7) != 0)) return Status::NotSupported;
+  if (desc.bias != nullptr && !aligned16(desc.bias)) return Status::NotSupported;
+  const int64_t rows_per_part = desc.m / parts;
+  const zcb::PersistentConfig want = zcb::choose_persistent(desc.m, desc.n, dev.sm_count);
+  const bool pair = want == zcb::PersistentConfig::Pair256x256 && rows_per_part % 256 == 0;
+  if (!pair && rows_per_part % 128 != 0) return Status::NotSupported;
+
+  zcb::LaunchArgs la{};
+  la.m = desc.m;
+  la.n = desc.n;
+  la.k = desc.k;
+  la.a = a_parts[0];
+  la.lda = desc.lda;
+  la.b = B;
+  la.ldb = desc.ldb;
+  la.c = desc.beta != 0.0f ? C : nullptr;
+  la.ldc = desc.ldc;
+  la.d = D;
+  la.ldd = desc.ldd;
+  la.bias = desc.bias;
+  la.alpha = desc.alpha;
+  la.beta = desc.beta;
+  la.bf16 = desc.a_type == DType::BF16;
+  la.b_col_major = true;
+  la.stream = desc.stream;
+  la.a_parts = a_parts;
+  la.a_nparts = parts;
+  la.a_rows_per_part = rows_per_part;
+  const cudaError_t e = pair ? zcb::launch_umma_pair_gemm(la)
+                             : zcb::launch_umma_gemm(la, want == zcb::PersistentConfig::Cta128x128 ? 128 : 256);
+  if (e == cudaErrorInvalidValue) return Status::NotSupported;
+  return e == cudaSuccess ? Status::Success : Status::RuntimeError;
+}
+
 Status gemm(const gemm_api::GemmArguments& args) {
   return gemm(desc_from_arguments(args), args.A.data, args.B.data, args.C.data, args.D.data);
 }

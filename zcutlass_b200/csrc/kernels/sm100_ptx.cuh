@@ -30,6 +30,29 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 
 __device__ __forceinline__ bool elect_lane0() { return (threadIdx.x & 31) == 0; }
 
+// Tensor maps of an operand whose rows are spread over kN buffers (a row block
+// per buffer, e.g. one per tensor-parallel rank in peer-mapped memory); kN = 1
+// is the ordinary single-buffer case. Passed by value as a __grid_constant__
+// kernel parameter, so each map lives in parameter space.
+template <int kN>
+struct TmaMapSet {
+  CUtensorMap map[kN];
+};
+
+// The map holding row `row` when rows are split into blocks of `rows_per_part`
+// (0 = one buffer).
+template <int kN>
+__device__ __forceinline__ const CUtensorMap* map_for_row(const TmaMapSet<kN>& set, int row, int rows_per_part,
+                                                         int parts) {
+  if constexpr (kN == 1) {
+    return &set.map[0];
+  } else {
+    int i = rows_per_part > 0 ? row / rows_per_part : 0;
+    i = i < parts - 1 ? i : parts - 1;
+    return &set.map[i < 0 ? 0 : i];
+  }
+}
+
 // Programmatic dependent launch. A kernel launched with programmatic stream
 // serialization may start while the previous kernel on its stream is still
 // running; griddep_wait() returns once that kernel has completed and its

@@ -39,6 +39,10 @@ struct UmmaGemmParams {
   int64_t ldd;
   uint32_t epi_flags;
   int* error_word;
+  // A split by rows over several buffers (TmaMapSet): rows [i * a_rows_per_part,
+  // (i + 1) * a_rows_per_part) come from map i. 0 / 1 for a single buffer.
+  int a_rows_per_part;
+  int a_parts;
 };
 
 namespace umma {
@@ -123,9 +127,9 @@ __device__ __forceinline__ void store_row_prefix(T* dst, const uint32_t (&packed
 
 // kBKMajor: B is given column-major (B[k][n] at n*ldb + k, i.e. a PyTorch
 // [N, K] weight); its tiles are then K-major like A's.
-template <typename T, int BN, int STAGES, bool kBKMajor>
+template <typename T, int BN, int STAGES, bool kBKMajor, int kAParts = 1>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+    gemm_kernel(const __grid_constant__ TmaMapSet<kAParts> amaps, const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_d, const UmmaGemmParams p) {
   using L = Smem<BN, STAGES>;
   constexpr uint32_t kTmemCols = tmem_cols_for(BN);
@@ -157,7 +161,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbarrier_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmap_a);
+    for (int i = 0; i < kAParts; ++i) tma_prefetch_desc(&amaps.map[i]);
     tma_prefetch_desc(&tmap_b);
     tma_prefetch_desc(&tmap_d);
   }
@@ -182,6 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int tm, tn;
         raster_tile(tile, p, tm, tn);
         const int m0 = tm * kBlockM, n0 = tn * BN;
+        const CUtensorMap* tmap_a = map_for_row(amaps, m0, p.a_rows_per_part, p.a_parts);
         for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
           const uint32_t s = it % STAGES;
           if (!mbar_wait(&empty[s], ((it / STAGES) & 1u) ^ 1u, ctx, kErrProducerEmpty)) {
@@ -189,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[s], L::kStageBytes);
-          tma_load_2d(smem + L::kAOff + s * L::kABytes, &tmap_a, &full[s], kb * kBlockK, m0);
+          tma_load_2d(smem + L::kAOff + s * L::kABytes, tmap_a, &full[s], kb * kBlockK, m0);
           if constexpr (kBKMajor) {
             tma_load_2d(smem + L::kBOff + s * L::kBBytes, &tmap_b, &full[s], kb * kBlockK, n0);
           } else {

@@ -61,9 +61,9 @@ enum : int {
   kErrEpiTmemFull = (11 << 4) | 3,
 };
 
-template <typename T, int STAGES, bool kBKMajor>
+template <typename T, int STAGES, bool kBKMajor, int kAParts = 1>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+    gemm_kernel(const __grid_constant__ TmaMapSet<kAParts> amaps, const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_d, const UmmaGemmParams p) {
   using L = Smem<STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbarrier_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmap_a);
+    for (int i = 0; i < kAParts; ++i) tma_prefetch_desc(&amaps.map[i]);
     tma_prefetch_desc(&tmap_b);
     tma_prefetch_desc(&tmap_d);
   }
@@ -124,6 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma::raster_tile(tile, p, tm, tn);
         const int m0 = tm * kBlockM + static_cast<int>(rank) * kHalfM;
         const int nb = tn * kBlockN + static_cast<int>(rank) * kHalfN;
+        const CUtensorMap* tmap_a = map_for_row(amaps, m0, p.a_rows_per_part, p.a_parts);
         for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
           const uint32_t s = it % STAGES;
           if (!mbar_wait(&empty[s], ((it / STAGES) & 1u) ^ 1u, ctx, kErrProducerEmpty)) {
@@ -132,7 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint32_t full_leader = map_shared_rank(smem_addr(&full[s]), 0);
           if (leader) mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);
-          tma_load_2d_pair(smem + L::kAOff + s * L::kABytes, &tmap_a, full_leader, kb * kBlockK, m0);
+          tma_load_2d_pair(smem + L::kAOff + s * L::kABytes, tmap_a, full_leader, kb * kBlockK, m0);
           uint8_t* sb = smem + L::kBOff + s * L::kBBytes;
           if constexpr (kBKMajor) {
             tma_load_2d_pair(sb, &tmap_b, full_leader, kb * kBlockK, nb);

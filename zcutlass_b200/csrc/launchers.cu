@@ -92,15 +92,28 @@ cudaError_t ensure_smem_attr(DeviceSlot* slot, int config_bit, Kernel kernel, in
   return e;
 }
 
-template <typename T, int BN, int STAGES, bool KM>
+// The A tensor maps: one for the single buffer, or one per row block when
+// the rows come from several buffers (a.a_nparts > 1).
+template <int AP>
+bool make_a_maps(TmaMapSet<AP>* set, const LaunchArgs& a, int box_rows, int box_k) {
+  const int parts = AP == 1 ? 1 : a.a_nparts;
+  if (parts < 1 || parts > AP) return false;
+  for (int i = 0; i < AP; ++i) {
+    const void* base = AP == 1 ? a.a : a.a_parts[i < parts ? i : 0];
+    if (!make_tma_2d(&set->map[i], base, a.bf16, a.m, a.k, a.lda, box_rows, box_k, TmaSwizzle::B128)) return false;
+  }
+  return true;
+}
+
+template <typename T, int BN, int STAGES, bool KM, int AP = 1>
 cudaError_t launch_umma_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit) {
   using L = umma::Smem<BN, STAGES>;
-  CUtensorMap ta, tb, td;
+  TmaMapSet<AP> ta;
+  CUtensorMap tb, td;
   const bool bf16 = a.bf16;
   const bool b_ok = KM ? make_tma_2d(&tb, a.b, bf16, a.n, a.k, a.ldb, BN, umma::kBlockK, TmaSwizzle::B128)
                        : make_tma_2d(&tb, a.b, bf16, a.k, a.n, a.ldb, umma::kBlockK, 64, TmaSwizzle::B128);
-  if (!b_ok ||
-      !make_tma_2d(&ta, a.a, bf16, a.m, a.k, a.lda, umma::kBlockM, umma::kBlockK, TmaSwizzle::B128) ||
+  if (!b_ok || !make_a_maps(&ta, a, umma::kBlockM, umma::kBlockK) ||
       !make_tma_2d(&td, a.d, bf16, a.m, a.n, a.ldd, 32, umma::kEpiCols, TmaSwizzle::B64)) {
     return cudaErrorInvalidValue;
   }
@@ -122,8 +135,10 @@ cudaError_t launch_umma_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit)
   p.ldd = a.ldd;
   p.epi_flags = (a.beta != 0.0f ? kEpiHasC : 0u) | (a.bias != nullptr ? kEpiHasBias : 0u);
   p.error_word = slot->info.error_word;
+  p.a_rows_per_part = AP == 1 ? 0 : static_cast<int>(a.a_rows_per_part);
+  p.a_parts = AP == 1 ? 1 : a.a_nparts;
 
-  auto kernel = umma::gemm_kernel<T, BN, STAGES, KM>;
+  auto kernel = umma::gemm_kernel<T, BN, STAGES, KM, AP>;
   cudaError_t e = ensure_smem_attr(slot, config_bit, kernel, L::kDynamicBytes);
   if (e != cudaSuccess) return e;
   const int grid = std::min(p.total_tiles, slot->info.sm_count);
@@ -198,16 +213,16 @@ cudaError_t launch_swapab_t(const LaunchArgs& a, DeviceSlot* slot, int config_bi
   return cudaGetLastError();
 }
 
-template <typename T, int STAGES, bool KM>
+template <typename T, int STAGES, bool KM, int AP = 1>
 cudaError_t launch_umma2_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit) {
   using L = umma2::Smem<STAGES>;
-  CUtensorMap ta, tb, td;
+  TmaMapSet<AP> ta;
+  CUtensorMap tb, td;
   const bool bf16 = a.bf16;
   const bool b_ok =
       KM ? make_tma_2d(&tb, a.b, bf16, a.n, a.k, a.ldb, umma2::kHalfN, umma2::kBlockK, TmaSwizzle::B128)
          : make_tma_2d(&tb, a.b, bf16, a.k, a.n, a.ldb, umma2::kBlockK, 64, TmaSwizzle::B128);
-  if (!b_ok ||
-      !make_tma_2d(&ta, a.a, bf16, a.m, a.k, a.lda, umma2::kHalfM, umma2::kBlockK, TmaSwizzle::B128) ||
+  if (!b_ok || !make_a_maps(&ta, a, umma2::kHalfM, umma2::kBlockK) ||
       !make_tma_2d(&td, a.d, bf16, a.m, a.n, a.ldd, 32, umma2::kEpiCols, TmaSwizzle::B64)) {
     return cudaErrorInvalidValue;
   }
@@ -229,8 +244,10 @@ cudaError_t launch_umma2_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit
   p.ldd = a.ldd;
   p.epi_flags = (a.beta != 0.0f ? kEpiHasC : 0u) | (a.bias != nullptr ? kEpiHasBias : 0u);
   p.error_word = slot->info.error_word;
+  p.a_rows_per_part = AP == 1 ? 0 : static_cast<int>(a.a_rows_per_part);
+  p.a_parts = AP == 1 ? 1 : a.a_nparts;
 
-  auto kernel = umma2::gemm_kernel<T, STAGES, KM>;
+  auto kernel = umma2::gemm_kernel<T, STAGES, KM, AP>;
   cudaError_t e = ensure_smem_attr(slot, config_bit, kernel, L::kDynamicBytes);
   if (e != cudaSuccess) return e;
 
@@ -415,6 +432,13 @@ enum : int {
   kCfgSkF16M32,
   kCfgSkBf16M64,
   kCfgSkF16M64,
+  // row-gathered A (column-major B only)
+  kCfgGatherPairBf16,
+  kCfgGatherPairF16,
+  kCfgGatherUmmaBf16N256,
+  kCfgGatherUmmaF16N256,
+  kCfgGatherUmmaBf16N128,
+  kCfgGatherUmmaF16N128,
   kCfgColMajorB = 32,
 };
 
@@ -508,12 +532,26 @@ int swapab_choose_splits(int64_t n, int64_t k, int sm_count) {
 cudaError_t launch_umma_gemm(const LaunchArgs& a, int bn) {
   DeviceSlot* slot = current_slot();
   if (slot == nullptr) return cudaErrorInvalidDevice;
+  if (a.a_nparts > 1) {
+    if (!a.b_col_major || a.a_nparts > kMaxAParts) return cudaErrorInvalidValue;
+    if (bn == 256) {
+      return a.bf16 ? launch_umma_t<__nv_bfloat16, 256, 4, true, kMaxAParts>(a, slot, kCfgGatherUmmaBf16N256)
+                    : launch_umma_t<half, 256, 4, true, kMaxAParts>(a, slot, kCfgGatherUmmaF16N256);
+    }
+    return a.bf16 ? launch_umma_t<__nv_bfloat16, 128, 6, true, kMaxAParts>(a, slot, kCfgGatherUmmaBf16N128)
+                  : launch_umma_t<half, 128, 6, true, kMaxAParts>(a, slot, kCfgGatherUmmaF16N128);
+  }
   return a.b_col_major ? launch_umma_km<true>(a, slot, bn) : launch_umma_km<false>(a, slot, bn);
 }
 
 cudaError_t launch_umma_pair_gemm(const LaunchArgs& a) {
   DeviceSlot* slot = current_slot();
   if (slot == nullptr) return cudaErrorInvalidDevice;
+  if (a.a_nparts > 1) {
+    if (!a.b_col_major || a.a_nparts > kMaxAParts) return cudaErrorInvalidValue;
+    return a.bf16 ? launch_umma2_t<__nv_bfloat16, 6, true, kMaxAParts>(a, slot, kCfgGatherPairBf16)
+                  : launch_umma2_t<half, 6, true, kMaxAParts>(a, slot, kCfgGatherPairF16);
+  }
   const int off = a.b_col_major ? kCfgColMajorB : 0;
   if (a.b_col_major) {
     return a.bf16 ? launch_umma2_t<__nv_bfloat16, 6, true>(a, slot, kCfgPairBf16 + off)

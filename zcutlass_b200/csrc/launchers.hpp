@@ -23,7 +23,15 @@ struct LaunchArgs {
   bool bf16;
   bool b_col_major;  // B[k][n] at n*ldb + k (PyTorch [N, K] weight)
   cudaStream_t stream;
+  // Rows of A gathered from several buffers (persistent kernels, column-major
+  // B): rows [i * a_rows_per_part, (i + 1) * a_rows_per_part) are read from
+  // a_parts[i], each a full [M, K] matrix with leading dimension lda.
+  const void* const* a_parts = nullptr;
+  int a_nparts = 0;
+  int64_t a_rows_per_part = 0;
 };
+
+constexpr int kMaxAParts = 8;
 
 // Per-device facts, cached on first use.
 struct DeviceInfo {
@@ -66,6 +74,13 @@ int swapab_choose_splits(int64_t n, int64_t k, int sm_count);
 // rank's barrier count.
 cudaError_t launch_nvls_allreduce(void* mc_ptr, int64_t nbytes, bool bf16, uint32_t* mc_flag, uint32_t* flag,
                                   int rank, int world, cudaStream_t stream);
+// The cross-rank barrier alone (same words and contract as the collectives).
+cudaError_t launch_nvls_barrier(uint32_t* mc_flag, uint32_t* flag, int world, cudaStream_t stream);
+// Reduce-scatter with the same barriers: rank r sums bytes
+// [r * nbytes / world, (r + 1) * nbytes / world) over all ranks into its own
+// copy at local_ptr (nbytes a multiple of 16 * world).
+cudaError_t launch_nvls_reduce_scatter(void* mc_ptr, void* local_ptr, int64_t nbytes, bool bf16, uint32_t* mc_flag,
+                                       uint32_t* flag, int rank, int world, cudaStream_t stream);
 int read_and_clear_error_word(bool clear);
 // Stream-K decode GEMM with its scratch in a fixed device array (no
 // allocation); returns a zcutlass status code. Arguments must already have
