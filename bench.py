@@ -283,16 +283,32 @@ def run_gpu(args) -> int:
         comm = "nvls" if want_nvls and layer.enable_nvls(TOKENS, lanes=micro) else "nccl"
     streams = [torch.cuda.Stream(device) for _ in range(micro)] if micro > 1 else None
     args.micro_used = micro
+    lane_rows = TOKENS // micro
+    # sequence-parallel layer: activations row-sharded between the linears,
+    # reduce-scatters instead of all-reduces, the gathers fused into the GEMMs
+    sp = bool(args.sp) and comm == "nvls" and TOKENS % micro == 0 and layer.enable_sequence_parallel(TOKENS, micro)
+    g = torch.Generator(device="cpu").manual_seed(1)
+    x_host = torch.randn(TOKENS, LLAMA3_8B.hidden, generator=g).to(torch.bfloat16)
+    x = x_host.to(device)
+    if sp:
+        # every rank holds every input row (each GEMM reads a row block from its
+        # owner); lane 0 holds all rows for the sequential breakdown pass
+        for j in range(micro):
+            rows = TOKENS if j == 0 else lane_rows
+            layer.sp_inputs[j].bufs[0][:rows].copy_(x[j * lane_rows: j * lane_rows + rows])
+        torch.cuda.synchronize()
+        dist.barrier()
 
     def step(xx, evs=None, outs=None):
         """One layer step; returns (row offset, output block) pieces."""
+        if sp:
+            if streams is not None:
+                return [(j * lane_rows, y) for j, y in enumerate(layer.forward_sp_overlapped(lane_rows, streams))]
+            return [(0, layer.forward_sp(TOKENS, events=evs))]
         if streams is not None:
             ys = layer.forward_overlapped(xx, streams, outs)
             return [(shard_range(xx.shape[0], j, micro)[0], y) for j, y in enumerate(ys)]
         return [(0, layer.forward(xx, events=evs, out=None if outs is None else outs[0]))]
-    g = torch.Generator(device="cpu").manual_seed(1)
-    x_host = torch.randn(TOKENS, LLAMA3_8B.hidden, generator=g).to(torch.bfloat16)
-    x = x_host.to(device)
 
     def barrier():
         if world > 1:
@@ -312,15 +328,19 @@ def run_gpu(args) -> int:
     # At TP > 1 the step is replayed from a CUDA graph: its ~20 launches are
     # host-bound otherwise (the GEMMs of a TP8 step last tens of microseconds).
     use_graph = args.graph == "on" or (args.graph == "auto" and world > 1)
-    graph, launches_per_step = None, None
+    graphs, launches_per_step = [], None
     if use_graph:
-        graph = torch.cuda.CUDAGraph()
-        l0 = _native.kernel_launches()
-        with torch.cuda.graph(graph, capture_error_mode="thread_local"):
-            step(x)
-        launches_per_step = _native.kernel_launches() - l0
-        for _ in range(3):
-            graph.replay()
+        # the sequence-parallel step must not reuse an output buffer on
+        # consecutive steps (other ranks read it), so it is captured twice
+        for _ in range(2 if sp else 1):
+            gr = torch.cuda.CUDAGraph()
+            l0 = _native.kernel_launches()
+            with torch.cuda.graph(gr, capture_error_mode="thread_local"):
+                step(x)
+            launches_per_step = _native.kernel_launches() - l0
+            graphs.append(gr)
+        for i in range(4):
+            graphs[i % len(graphs)].replay()
         barrier()
 
     # ---- device-timed steps (inputs resident in HBM)
@@ -331,20 +351,20 @@ def run_gpu(args) -> int:
         barrier()
         start.record()
         for i in range(args.steps):
-            if graph is not None:
-                graph.replay()
+            if graphs:
+                graphs[i % len(graphs)].replay()
             else:
                 step(x, {"gate_up": ev[i]})
         end.record()
         torch.cuda.synchronize()
     launches = _native.kernel_launches() - launches0
-    if graph is not None:  # replays launch what the capture recorded
+    if graphs:  # replays launch what the capture recorded
         launches = launches_per_step * args.steps
     ms = max_over_ranks(start.elapsed_time(end)) / args.steps
     barrier()
     total_flops = LLAMA3_8B.flops(TOKENS)
     value = total_flops / (ms * 1e-3) / 1e12
-    live_gate = streams is None and graph is None
+    live_gate = streams is None and not graphs
     if live_gate:
         gate_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
     gate_flops = 2.0 * TOKENS * layer.gate_up.weight.shape[0] * layer.gate_up.weight.shape[1]
@@ -354,7 +374,10 @@ def run_gpu(args) -> int:
     bev = [{nm: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for nm in names}
            for _ in range(20)]
     for evs in bev:
-        layer.forward(x, events=evs)
+        if sp:
+            layer.forward_sp(TOKENS, events=evs)
+        else:
+            layer.forward(x, events=evs)
     torch.cuda.synchronize()
     breakdown = {nm: round(max_over_ranks(statistics.mean(e[nm][0].elapsed_time(e[nm][1]) for e in bev)), 4)
                  for nm in names}
@@ -368,7 +391,11 @@ def run_gpu(args) -> int:
         b_layout=_native.COLUMN_MAJOR))["kernel_name"]
 
     # ---- end to end through the C ABI with pinned host buffers
-    e2e = run_e2e(args, layer, step, x_host, device, barrier, max_over_ranks, total_flops, use_graph)
+    if sp:
+        e2e = run_e2e_sp(args, layer, streams, lane_rows, x_host, device, barrier, max_over_ranks, total_flops,
+                         use_graph)
+    else:
+        e2e = run_e2e(args, layer, step, x_host, device, barrier, max_over_ranks, total_flops, use_graph)
 
     line = None
     if rank == 0:
@@ -380,6 +407,7 @@ def run_gpu(args) -> int:
                "allreduce": {"nvls": "zcutlass_nvls_allreduce (multimem.ld_reduce acc::f32 + multimem.st)",
                              "nccl": f"NCCL all_reduce, {args.chunks} row chunks", "none": "none (TP1)"}[comm],
                "micro_batches": micro, "cuda_graph": use_graph,
+               "sequence_parallel": sp,
                "order": "qkv -> o_proj (+all-reduce) -> gate_up -> down (+all-reduce)"}
         sm = clocks.summary()
         line = {
@@ -411,7 +439,7 @@ def run_gpu(args) -> int:
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
-        graph = None  # release the captured graph (it may hold NCCL calls) first
+        graphs.clear()  # release the captured graphs (they may hold NCCL calls) first
         torch.cuda.synchronize()
         barrier()
         dist.destroy_process_group()
@@ -515,6 +543,98 @@ def run_e2e(args, layer, step, x_host, device, barrier, max_over_ranks, total_fl
             "api": "C ABI zcutlass_gemm (include/zcutlass_c.h) via zcutlass_b200.tp"}
 
 
+def run_e2e_sp(args, layer, streams, lane_rows, x_host, device, barrier, max_over_ranks, total_flops,
+               use_graph=False) -> dict:
+    """End to end for the sequence-parallel step: each rank copies only its own
+    input rows of every row block from pinned host memory into the block's
+    input buffer (three rotate), a cross-rank barrier makes every rank's rows
+    visible, the step runs (qkv reads the other rows from their owners), and
+    each rank copies its own output rows back. No all-gather is needed."""
+    import torch
+
+    from zcutlass_b200.tp import shard_range
+
+    world, rank = layer.tp.world_size, layer.tp.rank
+    micro = len(streams) if streams is not None else 1
+    compute = torch.cuda.current_stream(device)
+    h2d_s, d2h_s = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    hidden = x_host.shape[1]
+    r0, r1 = shard_range(lane_rows, rank, world)
+    hx = [x_host[j * lane_rows + r0: j * lane_rows + r1].contiguous().pin_memory() for j in range(micro)]
+    hout = [[torch.empty(r1 - r0, layer.shape.hidden, dtype=x_host.dtype).pin_memory() for _ in range(micro)]
+            for _ in range(2)]
+    e = lambda: torch.cuda.Event()  # noqa: E731
+    h2d_ev, comp_ev, d2h_ev = [e() for _ in range(3)], [e() for _ in range(3)], [e(), e()]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def h2d(t):
+        with torch.cuda.stream(h2d_s):
+            for j in range(micro):
+                layer.sp_inputs[j].bufs[t % 3][r0:r1].copy_(hx[j], non_blocking=True)
+        h2d_ev[t % 3].record(h2d_s)
+
+    def compute_part(xi):
+        layer.sp_inputs[0].barrier()  # every rank's input rows for this step are in
+        if streams is not None:
+            return layer.forward_sp_overlapped(lane_rows, streams, xi)
+        return [layer.forward_sp(lane_rows, xi)]
+
+    graphs, graph_res = [], []
+
+    def loop(n):
+        start.record(compute)
+        h2d_s.wait_event(start)
+        h2d(0)
+        for t in range(n):
+            xi = t % 3
+            compute.wait_event(h2d_ev[xi])
+            if t >= 2:
+                compute.wait_event(d2h_ev[t % 2])
+            if graphs:
+                graphs[xi].replay()
+                ys = graph_res[xi]
+            else:
+                ys = compute_part(xi)
+            comp_ev[xi].record(compute)
+            if t + 1 < n:
+                # input buffer (t+1) % 3 was last read by the ranks at step t-2;
+                # this rank's step t-1 (its barriers) proves every rank is past it
+                if t >= 1:
+                    h2d_s.wait_event(comp_ev[(t - 1) % 3])
+                h2d(t + 1)
+            d2h_s.wait_event(comp_ev[xi])
+            with torch.cuda.stream(d2h_s):
+                for j in range(micro):
+                    hout[t % 2][j].copy_(ys[j][r0:r1], non_blocking=True)
+            d2h_ev[t % 2].record(d2h_s)
+        compute.wait_event(d2h_ev[(n - 1) % 2])
+        end.record(compute)
+        torch.cuda.synchronize()
+
+    loop(3)
+    barrier()
+    if use_graph:  # one graph per input buffer; the row-parallel buffers rotate in step
+        for xi in range(3):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                graph_res.append(compute_part(xi))
+            graphs.append(g)
+        loop(3)
+        barrier()
+    loop(args.steps)
+    ms = max_over_ranks(start.elapsed_time(end)) / args.steps
+    barrier()
+    graphs.clear()
+    torch.cuda.synchronize()
+    m = lane_rows * micro
+    return {"value": round(total_flops / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
+            "h2d_bytes_per_step": m * hidden * x_host.element_size(),
+            "d2h_bytes_per_step": m * layer.shape.hidden * x_host.element_size(),
+            "copies": "whole job: each rank copies its own input rows (H2D) and its own output rows (D2H); "
+                      "no all-gather (the GEMMs read peer rows)",
+            "api": "C ABI zcutlass_gemm_gather_a / zcutlass_nvls_reduce_scatter via zcutlass_b200.tp"}
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -526,6 +646,8 @@ def main(argv=None) -> int:
                     help="independent row blocks per step, each on its own stream (0: 2 when TP > 1, else 1)")
     ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",
                     help="replay each step from a CUDA graph (auto: when TP > 1)")
+    ap.add_argument("--sp", type=int, default=0,
+                    help="1: sequence-parallel layer (reduce-scatters, all-gathers fused into the GEMMs; NVLS only)")
     ap.add_argument("--comm", choices=["auto", "nvls", "nccl"], default="auto",
                     help="row-parallel all-reduce: the library's NVLS kernel or NCCL (auto: NVLS from TP4 up; "
                          "at TP2 NVLS moves 1.5x the bytes of a ring and NCCL is faster)")

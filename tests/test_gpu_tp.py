@@ -43,3 +43,4 @@ def test_tensor_parallel_multi_gpu(tmp_path):
     if "nvls_unavailable" not in rep:
         assert rep["nvls_allreduce"]["calls"] == 6
         assert rep["row_parallel_nvls"]["bound_ratio"] <= 1.0
+        assert rep["sequence_parallel"]["rel_frobenius"] < 1e-3

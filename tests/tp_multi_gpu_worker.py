@@ -8,7 +8,10 @@ Checks, against the CPU oracle:
   * RowParallelLinear over the NVLS all-reduce and over NCCL: within the error
     of rounding each rank's partial GEMM to bf16 before the sum;
   * ColumnParallelLinear: each rank's column shard passes the single-GPU
-    GEMM bounds.
+    GEMM bounds;
+  * the layer chain: two overlapped row blocks and graph replays against the
+    sequential run, and the sequence-parallel step against the all-reduce
+    step.
 Rank 0 writes a JSON report to argv[1]; any failure raises (non-zero exit).
 """
 
@@ -145,6 +148,45 @@ def check_layer_overlap(tp: TPGroup, dev, use_nvls: bool) -> dict:
     return {"exact_fraction": exact, "rel_frobenius": rel, "graph_replays_exact": graph_exact}
 
 
+def check_sequence_parallel(tp: TPGroup, dev) -> dict:
+    """The sequence-parallel step (reduce-scatters, and qkv / gate_up reading
+    their A rows from the owning ranks inside the GEMM) gives this rank's rows
+    of the all-reduce step's output; two overlapped lanes and a CUDA graph
+    replay give the same bits."""
+    shape = LayerShape(hidden=1024, intermediate=2048, q_heads=8, kv_heads=2, head_dim=128)
+    layer = TPDecoderLinears(shape, tp, dev, torch.bfloat16, seed=4, chunks=2)
+    rows = 256 * tp.world_size
+    assert layer.enable_sequence_parallel(rows, lanes=2), f"sequence parallel unavailable: {NvlsReducer.last_error}"
+    g = torch.Generator().manual_seed(99)
+    x = torch.randn(rows, shape.hidden, generator=g).to(torch.bfloat16).to(dev)
+    for lane in range(2):
+        layer.sp_inputs[lane].bufs[0][:rows].copy_(x)  # every rank holds all rows; each reads its owners'
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    ref = layer.forward(x).clone()  # all-reduce path
+    r0, r1 = shard_range(rows, tp.rank, tp.world_size)
+    y = layer.forward_sp(rows)[r0:r1].clone()
+    torch.cuda.synchronize(dev)
+    exact = float((y == ref[r0:r1]).float().mean())
+    rel = float((y.float() - ref[r0:r1].float()).norm() / ref[r0:r1].float().norm())
+    assert rel < 1e-3, f"sequence-parallel vs all-reduce step: rel {rel}"
+    streams = [torch.cuda.Stream(dev) for _ in range(2)]
+    for _ in range(3):
+        ys = [t[r0:r1].clone() for t in layer.forward_sp_overlapped(rows, streams)]
+        torch.cuda.synchronize(dev)
+        assert all(torch.equal(t, y) for t in ys), "overlapped sequence-parallel lanes differ"
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+        outs = layer.forward_sp_overlapped(rows, streams)
+    for _ in range(3):
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        assert all(torch.equal(t[r0:r1], y) for t in outs), "graph replay of the sequence-parallel step differs"
+    del graph
+    assert _native.device_error(True) == 0
+    return {"exact_fraction_vs_allreduce": exact, "rel_frobenius": rel}
+
+
 def main() -> None:
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -167,6 +209,7 @@ def main() -> None:
     report["layer_overlap_nccl"] = check_layer_overlap(tp, dev, False)
     if "nvls_unavailable" not in report:
         report["layer_overlap_nvls"] = check_layer_overlap(tp, dev, True)
+        report["sequence_parallel"] = check_sequence_parallel(tp, dev)
     torch.cuda.synchronize(dev)
     dist.barrier()
     if rank == 0:

@@ -17,7 +17,11 @@ vLLM. This module provides the same two shardings natively:
 
 TPDecoderLinears chains the four linears of one decoder layer;
 forward_overlapped() runs independent row blocks on separate streams so one
-block's all-reduce overlaps another block's GEMMs.
+block's all-reduce overlaps another block's GEMMs. forward_sp() is the
+sequence-parallel form of the same step: activations stay row-sharded between
+the linears, o_proj and down end in an NVLS reduce-scatter, and qkv / gate_up
+read the other ranks' rows inside the GEMM (zcutlass_gemm_gather_a: TMA loads
+from peer memory, no multicast), so no separate all-gather runs.
 
 Weights use the PyTorch [out_features, in_features] layout and go to the
 kernels as column-major B (no transposed copy). Every GEMM runs through the
@@ -97,42 +101,63 @@ class ColumnParallelLinear:
 
     __call__ = forward
 
+    def forward_gathered(self, x_parts: list[int], rows: int, out) -> None:
+        """out = x @ W_shard^T (+ b_shard) where x [rows, K] is sequence-sharded:
+        its row block r (rows / len(x_parts) rows) is read by the GEMM straight
+        from x_parts[r] -- a full [rows, K] buffer in rank r's memory -- with
+        no separate all-gather (zcutlass_gemm_gather_a)."""
+        import torch
+
+        from . import _native
+
+        k = self.weight.shape[1]
+        n = self.weight.shape[0]
+        t = _native.BF16 if self.weight.dtype == torch.bfloat16 else _native.F16
+        desc = _native.make_desc(rows, n, k, k, self.weight.stride(0), n, out.stride(0), t, 1.0, 0.0,
+                                 self.bias.data_ptr() if self.bias is not None else None,
+                                 torch.cuda.current_stream(out.device).cuda_stream, b_layout=_native.COLUMN_MAJOR)
+        st = _native.gemm_gather_a(desc, x_parts, self.weight.data_ptr(), None, out.data_ptr())
+        if st != _native.SUCCESS:
+            raise RuntimeError(f"zcutlass_gemm_gather_a failed: {_native.status_name(st)}")
+
 
 class NvlsReducer:
     """Row-parallel outputs in symmetric memory with an NVLink SHARP mapping.
 
-    Two symmetric buffers alternate between calls (the consumer of call i can
-    still be reading buffer i while call i+1 writes the other). `reduce`
+    Three symmetric buffers rotate between calls (the consumers of call i --
+    this rank's next GEMM, or other ranks reading rows of it -- can still be
+    reading buffer i while calls i+1 and i+2 write the others). `reduce`
     sums a partial in place across ranks with the library's NVLS all-reduce
     (zcutlass_nvls_allreduce: FP32 accumulation in the switch, one NVLink
     crossing per byte and direction), which brackets the reduction with its
     own bounded cross-rank barriers on two counter words kept in the same
-    symmetric allocation, after the two buffers. Every launch is fixed at
+    symmetric allocation, after the buffers. Every launch is fixed at
     issue time (no per-call values), so a step can be captured in a CUDA
     graph; each replay then alternates nothing -- the buffer a captured call
     uses is the one it used at capture."""
 
-    def __init__(self, max_rows: int, cols: int, dtype, device, group=None) -> None:
+    def __init__(self, max_rows: int, cols: int, dtype, device, group=None, nbufs: int = 3) -> None:
         import torch
         import torch.distributed as dist
         import torch.distributed._symmetric_memory as symm
 
         group = group or dist.group.WORLD
         self.dtype = dtype
+        self.nbufs = nbufs
         elem = torch.empty(0, dtype=dtype).element_size()
         region = -(-max_rows * cols * elem // 256) * 256
-        raw = symm.empty(2 * region + 256, dtype=torch.uint8, device=device)
+        raw = symm.empty(nbufs * region + 256, dtype=torch.uint8, device=device)
         self.handle = symm.rendezvous(raw, group)
         if not self.handle.multicast_ptr:
             raise RuntimeError("NVLS multicast is not available for this group")
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         self.raw = raw
         self.bufs = [raw[i * region: i * region + max_rows * cols * elem].view(dtype).view(max_rows, cols)
-                     for i in range(2)]
+                     for i in range(nbufs)]
         # multicast address = multicast base + offset of the local address in the allocation
         self.mc_base = self.handle.multicast_ptr - self.handle.buffer_ptrs[self.rank]
-        self.flag = raw.data_ptr() + 2 * region
-        raw[2 * region:].zero_()  # barrier counter and barrier count
+        self.flag = raw.data_ptr() + nbufs * region
+        raw[nbufs * region:].zero_()  # barrier counter and barrier count
         self.turn = 0
         torch.cuda.synchronize(device)
         dist.barrier(group)
@@ -150,8 +175,46 @@ class NvlsReducer:
 
     def next_buffer(self, rows: int):
         i = self.turn
-        self.turn ^= 1
+        self.turn = (self.turn + 1) % self.nbufs
         return i, self.bufs[i][:rows]
+
+    def peer_ptrs(self, i: int) -> list[int]:
+        """Address of buffer i in every rank's allocation (peer-mapped), by rank."""
+        off = self.bufs[i].data_ptr() - self.handle.buffer_ptrs[self.rank]
+        return [int(base) + off for base in self.handle.buffer_ptrs]
+
+    def _code(self):
+        import torch
+
+        from . import _native
+
+        return _native.BF16 if self.dtype == torch.bfloat16 else _native.F16
+
+    def barrier(self) -> None:
+        """Cross-rank barrier on the current stream (bounded, device-side)."""
+        import torch
+
+        from . import _native
+
+        st = _native.lib().zcutlass_nvls_barrier(self.mc_base + self.flag, self.flag, self.world,
+                                                 torch.cuda.current_stream().cuda_stream)
+        if st != _native.SUCCESS:
+            raise RuntimeError(f"zcutlass_nvls_barrier failed: {_native.status_name(st)}")
+
+    def reduce_scatter(self, i: int, rows: int) -> None:
+        """Rank r's rows [r * rows / W, (r + 1) * rows / W) of buffer i become
+        the sum over ranks, in place in its own copy (rows a multiple of W)."""
+        import torch
+
+        from . import _native
+
+        t = self.bufs[i]
+        nbytes = rows * t.shape[1] * t.element_size()
+        st = _native.lib().zcutlass_nvls_reduce_scatter(
+            self.mc_base + t.data_ptr(), t.data_ptr(), nbytes, self._code(), self.mc_base + self.flag, self.flag,
+            self.rank, self.world, torch.cuda.current_stream().cuda_stream)
+        if st != _native.SUCCESS:
+            raise RuntimeError(f"zcutlass_nvls_reduce_scatter failed: {_native.status_name(st)}")
 
     def reduce(self, i: int, rows: int) -> None:
         import torch
@@ -208,6 +271,10 @@ class RowParallelLinear:
             if int(ok.item()) == 1:
                 self.nvls_lanes.extend(made)
         return len(self.nvls_lanes) >= lanes
+
+    def partial(self, x_shard, out) -> None:
+        """This rank's un-reduced term x_shard @ W_shard^T (+ bias on rank 0) into out."""
+        self.linear_fn(x_shard, self.weight, self.bias if self.tp.rank == 0 else None, out)
 
     @classmethod
     def from_full(cls, weight, bias=None, tp: TPGroup | None = None, chunks: int = 4,
@@ -315,10 +382,98 @@ class TPDecoderLinears:
         self.o_cols = o_hi - o_lo
         self.d_cols = d_hi - d_lo
         self._bufs = {}
+        self.sp_inputs: list[NvlsReducer] = []  # set by enable_sequence_parallel()
 
     def enable_nvls(self, max_tokens: int, lanes: int = 1) -> bool:
         """Use the library's NVLS all-reduce for both row-parallel linears."""
         return self.o_proj.enable_nvls(max_tokens, lanes) and self.down.enable_nvls(max_tokens, lanes)
+
+    def enable_sequence_parallel(self, max_tokens: int, lanes: int = 1) -> bool:
+        """Symmetric buffers for forward_sp: the NVLS lanes of the row-parallel
+        linears plus, per lane, three rotating input buffers. Returns whether
+        every rank has them (else the all-reduce path stays in use)."""
+        import torch
+        import torch.distributed as dist
+
+        if self.tp.world_size < 2 or not self.enable_nvls(max_tokens, lanes):
+            return False
+        dev, dt = self.qkv.weight.device, self.qkv.weight.dtype
+        made = [NvlsReducer.try_create(max_tokens, self.shape.hidden, dt, dev, self.tp.group, nbufs=3)
+                for _ in range(lanes)]
+        ok = torch.tensor([0 if any(r is None for r in made) else 1], device=dev, dtype=torch.int32)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.tp.group)
+        self.sp_inputs = made if int(ok.item()) == 1 else []
+        return bool(self.sp_inputs)
+
+    def _sp_steps(self, rows: int, lane: int, xi: int, events: dict | None):
+        """The sequence-parallel chain of one block of `rows` tokens, as two
+        callables (through o_proj's reduce-scatter, then the rest). Rank r owns
+        rows [r * rows / W, (r + 1) * rows / W) of the block: its input rows
+        sit in buffer xi of the lane's input set, and it ends with the same
+        rows of the down output (the sum over ranks). qkv and gate_up read
+        the other ranks' rows straight from their buffers inside the GEMM;
+        o_proj and down end in an NVLS reduce-scatter."""
+        b = self.buffers(rows, self.qkv.weight.device, self.qkv.weight.dtype, lane)
+        x_in = self.sp_inputs[lane]
+        state = {}
+
+        def timed(name, fn):
+            if events is not None and name in events:
+                events[name][0].record()
+                r = fn()
+                events[name][1].record()
+                return r
+            return fn()
+
+        def o_proj():
+            red = self.o_proj.nvls_lanes[lane]
+            i, y = red.next_buffer(rows)
+            self.o_proj.partial(b["qkv"][:, : self.o_cols], y)
+            red.reduce_scatter(i, rows)
+            state["o"] = (red, i)
+
+        def down():
+            red = self.down.nvls_lanes[lane]
+            i, y = red.next_buffer(rows)
+            self.down.partial(b["gate_up"][:, : self.d_cols], y)
+            red.reduce_scatter(i, rows)
+            state["y"] = y
+
+        def first():
+            timed("qkv", lambda: self.qkv.forward_gathered(x_in.peer_ptrs(xi), rows, b["qkv"]))
+            timed("o_proj", o_proj)
+
+        def second():
+            red, i = state["o"]
+            timed("gate_up", lambda: self.gate_up.forward_gathered(red.peer_ptrs(i), rows, b["gate_up"]))
+            timed("down", down)
+
+        return first, second, state
+
+    def forward_sp(self, rows: int, xi: int = 0, events: dict | None = None):
+        """Sequence-parallel layer step on lane 0 (see _sp_steps); returns the
+        lane's down buffer, whose rows of this rank hold the result."""
+        first, second, state = self._sp_steps(rows, 0, xi, events)
+        first()
+        second()
+        return state["y"]
+
+    def forward_sp_overlapped(self, rows: int, streams, xi: int = 0):
+        """forward_sp over len(streams) lanes, each a block of `rows` tokens in
+        its own input set, issued interleaved on their own streams."""
+        import torch
+
+        cur = torch.cuda.current_stream(self.qkv.weight.device)
+        chains = [self._sp_steps(rows, j, xi, None) for j in range(len(streams))]
+        for s in streams:
+            s.wait_stream(cur)
+        for phase in (0, 1):
+            for j, s in enumerate(streams):
+                with torch.cuda.stream(s):
+                    chains[j][phase]()
+        for s in streams:
+            cur.wait_stream(s)
+        return [c[2]["y"] for c in chains]
 
     def flops_per_rank(self, tokens: int) -> float:
         q = self.qkv.weight.shape[0] * self.qkv.weight.shape[1]
