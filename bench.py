@@ -10,7 +10,9 @@ all-reduce of the BF16 partials: the library's NVLS kernel, or NCCL with
 --comm nccl). At TP > 1 the 8192 tokens run as two independent 4096-row
 blocks on two streams (--micro), so one block's all-reduce overlaps the other
 block's GEMMs. 3573 GFLOP per step for the whole job, whatever the rank
-count (strong scaling).
+count (strong scaling). --sp 1 runs the sequence-parallel form of the same
+step instead (reduce-scatters, with qkv / gate_up reading the other ranks'
+rows inside the GEMM; NVLS only).
 
     python bench.py                          # N=1, defaults
     torchrun --nproc-per-node N bench.py --gpus N --steps K --warmup W
@@ -479,7 +481,7 @@ def run_e2e(args, layer, step, x_host, device, barrier, max_over_ranks, total_fl
     def compute_part(s):
         if world > 1:
             dist.all_gather_into_tensor(dx[s], dx_part[s], group=layer.tp.group)
-        # NVLS keeps the output in its lanes' ping-pong symmetric buffers
+        # NVLS keeps the output in its lanes' rotating symmetric buffers
         return step(dx[s], outs=None if layer.down.nvls else [dout[s]] if streams_n == 1 else
                     [dout[s][p0:p1] for p0, p1 in blocks])
 

@@ -80,7 +80,7 @@ def check_row_parallel(tp: TPGroup, dev, use_nvls: bool) -> dict:
     if use_nvls:
         assert row.enable_nvls(m), f"NVLS unavailable: {NvlsReducer.last_error}"
     outs = []
-    for _ in range(3):  # repeated calls alternate the ping-pong buffers
+    for _ in range(3):  # repeated calls rotate the symmetric buffers
         outs.append(bits(row(from_bits(x[:, klo:khi], dev))))
     assert all(np.array_equal(outs[0], o) for o in outs[1:]), "row-parallel output changed between calls"
     ref = oracle.gemm(x, np.ascontiguousarray(w.T), m, n, k, BF16, bias=bias)
@@ -123,7 +123,7 @@ def check_layer_overlap(tp: TPGroup, dev, use_nvls: bool) -> dict:
     x = torch.randn(512, shape.hidden, generator=g).to(torch.bfloat16).to(dev)
     streams = [torch.cuda.Stream(dev) for _ in range(2)]
     seq = torch.cat([layer.forward(x[:256]).clone(), layer.forward(x[256:]).clone()])
-    for _ in range(3):  # several rounds: lanes alternate their ping-pong buffers
+    for _ in range(3):  # several rounds: lanes rotate their symmetric buffers
         ov = torch.cat([y.clone() for y in layer.forward_overlapped(x, streams)])
     torch.cuda.synchronize(dev)
     exact = float((ov == seq).float().mean())
