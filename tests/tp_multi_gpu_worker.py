@@ -13,6 +13,7 @@ Checks, against the CPU oracle:
     sequential run, and the sequence-parallel step against the all-reduce
     step.
 Rank 0 writes a JSON report to argv[1]; any failure raises (non-zero exit).
+An optional argv[2] of "sp" runs the sequence-parallel check alone.
 """
 
 from __future__ import annotations
@@ -196,18 +197,23 @@ def main() -> None:
     tp = TPGroup.from_env()
     report = {"world": world}
 
+    only = sys.argv[2] if len(sys.argv) > 2 else None  # "sp": the sequence-parallel check alone
     red = NvlsReducer.try_create(64, 1024, torch.bfloat16, dev, tp.group)
     ok = torch.tensor([0 if red is None else 1], device=dev, dtype=torch.int32)
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-    if int(ok.item()) == 1:
+    if only == "sp":
+        assert int(ok.item()) == 1, f"NVLS unavailable: {NvlsReducer.last_error}"
+        report["sequence_parallel"] = check_sequence_parallel(tp, dev)
+    elif int(ok.item()) == 1:
         report["nvls_allreduce"] = check_allreduce(red, rank, world, dev)
         report["row_parallel_nvls"] = check_row_parallel(tp, dev, True)
     else:
         report["nvls_unavailable"] = NvlsReducer.last_error or "another rank has no multicast"
-    report["row_parallel_nccl"] = check_row_parallel(tp, dev, False)
-    report["column_parallel"] = check_column_parallel(tp, dev)
-    report["layer_overlap_nccl"] = check_layer_overlap(tp, dev, False)
-    if "nvls_unavailable" not in report:
+    if only is None:
+        report["row_parallel_nccl"] = check_row_parallel(tp, dev, False)
+        report["column_parallel"] = check_column_parallel(tp, dev)
+        report["layer_overlap_nccl"] = check_layer_overlap(tp, dev, False)
+    if only is None and "nvls_unavailable" not in report:
         report["layer_overlap_nvls"] = check_layer_overlap(tp, dev, True)
         report["sequence_parallel"] = check_sequence_parallel(tp, dev)
     torch.cuda.synchronize(dev)
