@@ -123,9 +123,10 @@ uint64_t zcutlass_gemm_kernel_launches(void);
 
 /* Decode GEMM that allocates nothing (no counterpart in the reference).
  *
- * For callers that cannot call cudaMalloc: code running while a CUDA graph is
- * being captured or inside a custom allocator/memory-pool callback, or hosts
- * that forbid device allocation after start-up. The regular entry points may
+ * For callers that cannot call cudaMalloc: code inside a custom allocator or
+ * memory-pool callback (an allocation there would re-enter the allocator), and
+ * serving processes that reserve all device memory at start-up and forbid any
+ * device allocation afterwards. The regular entry points may
  * allocate a per-stream workspace the first time the stream-K decode kernel
  * runs on a stream; this one runs that kernel with its scratch in a fixed
  * 16 MiB array compiled into the library (every GPU that loads the library
@@ -136,9 +137,11 @@ uint64_t zcutlass_gemm_kernel_launches(void);
  *   B is [K,N] row-major (b_col_major = 0) or a [N,K] weight (b_col_major = 1).
  *
  * Limits: 1 <= M <= 64; A and B 16-byte aligned with lda, ldb multiples of 8;
- * scratch needed = 64 KiB of tile counters (N <= 1,048,576) + 2 * G * MP * 512
- * bytes of partials (G = min(#SMs, ceil(N/128) * ceil(K/128)), MP = 16, 32 or
- * 64 by M) must fit in 16 MiB. Anything outside these limits returns
+ * N <= 1,048,576 (8192 tile counters of 128 columns in the first 64 KiB).
+ * The FP32 partial tiles take 2 * G * MP * 512 bytes (G = min(#SMs,
+ * ceil(N/128) * ceil(K/128)), MP = 16, 32 or 64 by M): at most 9.7 MB on a
+ * 148-SM B200, always within the rest of the 16 MiB, so on B200 only M and N
+ * limit a call. Anything outside these limits returns
  * ZCUTLASS_INVALID_ARGUMENT without launching; other argument errors return
  * the same codes as zcutlass_gemm.
  * The first call on each device looks up the scratch array's device address

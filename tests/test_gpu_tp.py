@@ -44,3 +44,23 @@ def test_tensor_parallel_multi_gpu(tmp_path):
         assert rep["nvls_allreduce"]["calls"] == 6
         assert rep["row_parallel_nvls"]["bound_ratio"] <= 1.0
         assert rep["sequence_parallel"]["rel_frobenius"] < 1e-3
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("comm", ["auto", "nvls"])
+def test_bench_two_gpus_exits(comm):
+    """bench.py at TP2 as the driver launches it (one rank per GPU, CUDA graphs
+    holding the NCCL or NVLS all-reduces) prints its line and exits 0: every
+    captured graph is freed before the process group is destroyed."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 or more GPUs")
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           str(ROOT / "bench.py"), "--gpus", "2", "--steps", "3", "--warmup", "3", "--comm", comm]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=330, cwd=ROOT, env=dict(os.environ))
+    assert r.returncode == 0, f"rc {r.returncode}\nstdout:\n{r.stdout[-3000:]}\nstderr:\n{r.stderr[-5000:]}"
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, r.stdout[-3000:]
+    line = json.loads(lines[0])
+    assert line["n_gpus"] == 2 and line["value"] > 0 and line["e2e"]["value"] > 0
+    assert "teardown did not finish" not in r.stderr

@@ -1,19 +1,21 @@
 """The decode GEMM entry point that allocates nothing: zcutlass_gemm_decode_noalloc.
 
 Some callers cannot allocate device memory at the moment they call the GEMM:
-code running while a CUDA graph is being captured, code inside an allocator
-or memory-pool callback, and services that forbid device allocation after
-start-up. The regular entry points may allocate a per-stream workspace the
-first time the stream-K decode kernel runs on a stream; this entry point runs
-that kernel with its scratch in a fixed array compiled into the library.
+code inside an allocator or memory-pool callback (a cudaMalloc there would
+re-enter the allocator), and serving processes that reserve all device memory
+up front and forbid any allocation after start-up. The regular entry points
+may allocate a per-stream workspace the first time the stream-K decode kernel
+runs on a stream; this entry point runs that kernel with its scratch in a
+fixed array compiled into the library.
 
 The test calls it through the C ABI twice in a row -- the second call finds
 the first call's counters and partial tiles still in the shared scratch -- and
-checks both results against zcutlass_gemm on the same inputs, with the same
-tolerances as the other GPU tests. It also checks that repeated calls allocate
-no device memory, that problems beyond the scratch limit are rejected before
-any launch, and that zero-size problems succeed. The file name makes pytest
-collect it last; it also passes alone in a fresh process.
+checks both results against zcutlass_gemm on the same inputs and against the
+oracle, with the same tolerances as the other GPU tests. It also checks that
+repeated calls allocate no device memory, that problems beyond the scratch
+limit are rejected before any launch, and that zero-size problems succeed.
+The file name makes pytest collect it last; it also passes alone in a fresh
+process.
 """
 
 from __future__ import annotations
@@ -63,6 +65,10 @@ def test_noalloc_matches_gemm_twice(cuda_device, m, n, k, dtype, col, beta, with
     assert _native.gemm(desc, a.data_ptr(), w.data_ptr(), cptr, ref.data_ptr()) == _native.SUCCESS
     torch.cuda.synchronize()
     ref_np = ref.float().cpu().numpy()
+    # the oracle on the same bit patterns (B as the [K, N] row-major matrix it reads)
+    bits = lambda t: t.contiguous().cpu().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    oracle_ref = oracle.gemm(bits(a), bits(w.t() if col else w), m, n, k, dtype, c=bits(c) if beta != 0.0 else None,
+                             bias=bits(bias) if bias is not None else None, alpha=1.0, beta=beta)
 
     outs = []
     for call in range(2):
@@ -77,7 +83,8 @@ def test_noalloc_matches_gemm_twice(cuda_device, m, n, k, dtype, col, beta, with
             assert torch.cuda.mem_get_info()[0] == free_before
         assert _native.device_error(clear=True) == 0
         out = d.float().cpu().numpy()
-        oracle.check(out, ref_np.astype(np.float64), dtype)
+        oracle.check(out, ref_np.astype(np.float64), dtype)  # against zcutlass_gemm
+        oracle.check(out, oracle_ref, dtype)  # against the oracle
         outs.append(out)
     np.testing.assert_array_equal(outs[0], outs[1])  # the scratch left by call 1 does not leak into call 2
 

@@ -98,9 +98,14 @@ constexpr int kArMaxBlocks = 32;
 
 // Reduces 16-byte words [lo, lo + n) across all ranks. kBroadcast: the sums go
 // back to every rank's copy (all-reduce); otherwise only to this rank's copy
-// at `local` (reduce-scatter).
+// at `local` (reduce-scatter). When the device error word is already set --
+// the barrier before this launch gave up waiting, so some peers' partials may
+// be incomplete -- the kernel does nothing: the caller reads the error word
+// and must not use the buffer, and no half-reduced sum is written over it.
 template <bool kBf16, bool kBroadcast>
-__global__ void __launch_bounds__(kArThreads) nvls_reduce_kernel(uint8_t* mc, uint8_t* local, int64_t lo, int64_t n) {
+__global__ void __launch_bounds__(kArThreads) nvls_reduce_kernel(uint8_t* mc, uint8_t* local, int64_t lo, int64_t n,
+                                                                 const int* error_word) {
+  if (error_word != nullptr && *reinterpret_cast<const volatile int*>(error_word) != 0) return;
   uint8_t* base = mc + lo * 16;
   uint8_t* dst = local + lo * 16;
   const int64_t step = static_cast<int64_t>(gridDim.x) * kArThreads * kArUnroll;
@@ -169,11 +174,11 @@ cudaError_t launch_reduce(void* mc_ptr, void* local_ptr, int64_t lo, int64_t n, 
 
   nvls_barrier_kernel<<<1, 32, 0, stream>>>(mc_flag, flag, w, kWaitTimeoutNs, kErrNvlsBarrierPre, info->error_word);
   if (broadcast) {
-    if (bf16) nvls_reduce_kernel<true, true><<<grid, kArThreads, 0, stream>>>(mc, local, lo, n);
-    else nvls_reduce_kernel<false, true><<<grid, kArThreads, 0, stream>>>(mc, local, lo, n);
+    if (bf16) nvls_reduce_kernel<true, true><<<grid, kArThreads, 0, stream>>>(mc, local, lo, n, info->error_word);
+    else nvls_reduce_kernel<false, true><<<grid, kArThreads, 0, stream>>>(mc, local, lo, n, info->error_word);
   } else {
-    if (bf16) nvls_reduce_kernel<true, false><<<grid, kArThreads, 0, stream>>>(mc, local, lo, n);
-    else nvls_reduce_kernel<false, false><<<grid, kArThreads, 0, stream>>>(mc, local, lo, n);
+    if (bf16) nvls_reduce_kernel<true, false><<<grid, kArThreads, 0, stream>>>(mc, local, lo, n, info->error_word);
+    else nvls_reduce_kernel<false, false><<<grid, kArThreads, 0, stream>>>(mc, local, lo, n, info->error_word);
   }
   nvls_barrier_kernel<<<1, 32, 0, stream>>>(mc_flag, flag, w, kWaitTimeoutNs, kErrNvlsBarrierPost, info->error_word);
   count_launches(3);

@@ -645,9 +645,10 @@ int selftest_bounded_wait(uint32_t timeout_us) {
 
 // ---------------------------------------------------------------- decode without allocation
 //
-// Some callers cannot allocate device memory at call time (inside CUDA graph
-// capture, inside an allocator callback, or under a no-allocation-after-
-// start-up policy). For them the stream-K decode kernel can run with its
+// Some callers cannot allocate device memory at call time (inside an
+// allocator or memory-pool callback, or in a process that reserves all device
+// memory at start-up and allocates nothing afterwards). For them the stream-K
+// decode kernel can run with its
 // scratch -- tile counters and FP32 partial tiles -- in this fixed array
 // instead of the per-stream workspace. The array is part of the library
 // image: every device that loads the library holds it until exit.

@@ -51,6 +51,23 @@ class TPGroup:
         return cls(dist.get_rank(group), dist.get_world_size(group), group)
 
 
+def check_device_error() -> None:
+    """Raises if a kernel of the library recorded an error on the current
+    device since the last check (a bounded wait that gave up: an NVLS barrier
+    whose peers never arrived, or a GEMM pipeline wait). After such an error
+    the outputs of the steps since the last check must not be used: the NVLS
+    reduction skips its work once the error word is set. Reading the word
+    synchronises the device; call it between steps, not inside a capture."""
+    from . import _native
+
+    code = _native.device_error(clear=True)
+    if code < 0:
+        raise RuntimeError("zcutlass device error word unreadable: the device synchronisation failed")
+    if code != 0:
+        raise RuntimeError(f"zcutlass device error word 0x{code:x} (site {code >> 4}, role {code & 15}): "
+                           "a bounded wait gave up; the results since the last check are invalid")
+
+
 def shard_range(total: int, rank: int, world: int) -> tuple[int, int]:
     """Contiguous [start, stop) slice of `total` owned by `rank` (sizes differ by at most 1)."""
     base, rem = divmod(total, world)
