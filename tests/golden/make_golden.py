@@ -5,7 +5,7 @@ disabled, i.e. its `_fallback` (python/zcutlass_torch/overlay.py:130-145) for
 `gemm` and `torch.nn.functional.linear` for `linear` (overlay.py:218-231) --
 on seeded inputs, and stores inputs, outputs and the overlay's fallback
 counters as small fixtures. It must run where the reference checkout exists
-(default /root/reference, override with ZCUTLASS_REF_ROOT); the tests only
+(ZCUTLASS_REF_ROOT, else a `reference` directory beside this repository); the tests only
 read the .npz it writes.
 
     python tests/golden/make_golden.py
@@ -21,7 +21,7 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "reference_cpu_path.npz"
-REF_ROOT = Path(os.environ.get("ZCUTLASS_REF_ROOT", "/root/reference"))
+REF_ROOT = Path(os.environ.get("ZCUTLASS_REF_ROOT", HERE.parents[2] / "reference"))
 
 # The reference's numeric test cases (tests/test_gemm.cu:754-786), shrunk where
 # K*N would make the fixture large, plus LLM-shaped small cases.

@@ -20,7 +20,8 @@ import torch
 import zcutlass_torch
 from zcutlass_torch import OverlayStats, RoutingPolicy, ZCutlassGemmOverlay
 
-REF_OVERLAY = Path(os.environ.get("ZCUTLASS_REF_ROOT", "/root/reference")) / "python" / "zcutlass_torch" / "overlay.py"
+REF_ROOT = Path(os.environ.get("ZCUTLASS_REF_ROOT", Path(__file__).resolve().parents[2] / "reference"))
+REF_OVERLAY = REF_ROOT / "python" / "zcutlass_torch" / "overlay.py"
 
 
 def _reference_overlay_module():

@@ -1,23 +1,27 @@
-"""vLLM LinearMethod that routes selected Linear layers to zcutlass.
+"""vLLM LinearMethod that sends selected unquantized Linear layers to zcutlass.
 
-Mirrors ZCutlassUnquantizedLinearMethod (python/zcutlass_vllm/linear_method.py
-in supercatking/zcutlass): wraps vLLM's UnquantizedLinearMethod, decides misses
-from shapes before touching the weight (61-83), the measured profit policy
-ZCUTLASS_VLLM_PROFIT_POLICY and its reason strings (85-111), a transposed
-weight cache keyed on (data_ptr, shape, dtype, device) (113-134), apply()
-(136-161) and the installer (169-198).
+Public surface of the reference's method (python/zcutlass_vllm/linear_method.py
+in supercatking/zcutlass): ZCutlassUnquantizedLinearMethod (create_weights /
+process_weights_after_loading / apply, `stats`, `last_trace` with its
+`weight_cache` key), clear_zcutlass_weight_cache and
+install_zcutlass_unquantized_linear_method. apply() decides misses from the
+layer's shapes and the profit policy (ZCUTLASS_VLLM_PROFIT_POLICY) before the
+weight is touched, then runs the adapter on a [K, N] copy of the weight that
+is made once and reused while the weight's storage is unchanged.
 
 B200 addition (opt-in, native_weight_layout=True): the vLLM weight stays in
-its [N, K] layout and goes to the kernels as column-major B; no transposed
-copy is made or cached (trace key weight_cache = "native").
+its [N, K] layout and runs as column-major B, so no [K, N] copy exists
+(weight_cache = "native"); that removes the second copy of every routed
+weight from device memory.
 """
 
 from __future__ import annotations
 
-import os
+from dataclasses import dataclass
 from typing import Any, Optional
 
-from .linear import ZCutlassVllmLinearAdapter
+from ..routing import Rule, env_word, first_reason
+from .linear import SHAPE_RULES, LinearShape, ZCutlassVllmLinearAdapter, fast_reason
 
 try:  # vLLM is optional outside serving environments
     from vllm.model_executor.layers.linear import LinearMethodBase, UnquantizedLinearMethod
@@ -25,8 +29,76 @@ except Exception:  # pragma: no cover - exercised without vLLM
     LinearMethodBase = object  # type: ignore[assignment,misc]
     UnquantizedLinearMethod = None  # type: ignore[assignment]
 
+FALLBACK_PATH = "vllm_unquantized_fallback"
 
-_HALF_NAMES = ("torch.float16", "float16", "f16", "half", "torch.half")
+# ---------------------------------------------------------------- profit policy
+
+# Policy words that route everything the family policy allows.
+PASS_THROUGH_POLICIES = frozenset({"", "0", "off", "none", "false", "disabled", "all", "experimental"})
+HALF_DTYPE_NAMES = frozenset({"torch.float16", "float16", "f16", "half", "torch.half"})
+# The one (m, n, k) the reference measured as profitable: f16 prefill qkv_proj with bias.
+MEASURED_SHAPES = frozenset({(256, 2048, 1536)})
+
+
+@dataclass(frozen=True)
+class ProfitCase:
+    policy: str
+    dtype: str
+    family: str
+    has_bias: bool
+    prefix: str
+    mnk: tuple[int, int, int]
+
+
+# `measured` keeps only the profitable subset; reasons in the reference's
+# order (python/zcutlass_vllm/linear_method.py:85-111).
+PROFIT_RULES = (
+    Rule("profit_policy_unknown", lambda c: c.policy != "measured"),
+    Rule("profit_policy_dtype_not_promoted", lambda c: c.dtype not in HALF_DTYPE_NAMES),
+    Rule("profit_policy_family_not_promoted", lambda c: c.family != "prefill"),
+    Rule("profit_policy_bias_not_promoted", lambda c: not c.has_bias),
+    Rule("profit_policy_layer_not_promoted", lambda c: "qkv_proj" not in c.prefix),
+    Rule("profit_policy_shape_not_promoted", lambda c: c.mnk not in MEASURED_SHAPES),
+)
+
+
+def profit_policy() -> str:
+    return env_word("ZCUTLASS_VLLM_PROFIT_POLICY", "off")
+
+
+# ---------------------------------------------------------------- [K, N] weight copies
+
+_CACHE_ATTR = "_zcutlass_weight_t_cache"
+
+
+def _storage_key(weight) -> tuple:
+    """Changes whenever the weight's storage, shape, dtype or device does."""
+    ptr = int(weight.data_ptr()) if hasattr(weight, "data_ptr") else 0
+    return ptr, tuple(weight.shape), str(weight.dtype), str(weight.device)
+
+
+def transposed_weight(layer, enabled: bool = True) -> tuple[Any, str]:
+    """(contiguous [K, N] copy of layer.weight, how it was obtained: "hit",
+    "miss" (made and kept on the layer) or "disabled" (made, not kept))."""
+    w = layer.weight
+    if not enabled:
+        return w.t().contiguous(), "disabled"
+    key = _storage_key(w)
+    kept = getattr(layer, _CACHE_ATTR, None)
+    if kept is not None and kept[0] == key:
+        return kept[1], "hit"
+    copy = w.t().contiguous()
+    setattr(layer, _CACHE_ATTR, (key, copy))
+    return copy, "miss"
+
+
+def clear_zcutlass_weight_cache(layer) -> None:
+    """Drops the layer's kept [K, N] copy, if any."""
+    if hasattr(layer, _CACHE_ATTR):
+        delattr(layer, _CACHE_ATTR)
+
+
+# ---------------------------------------------------------------- the method
 
 
 class ZCutlassUnquantizedLinearMethod(LinearMethodBase):  # type: ignore[misc,valid-type]
@@ -44,13 +116,8 @@ class ZCutlassUnquantizedLinearMethod(LinearMethodBase):  # type: ignore[misc,va
         self.native_weight_layout = native_weight_layout
         self.last_weight_cache = "unknown"
 
-    @property
-    def stats(self):
-        return self.adapter.stats
-
-    @property
-    def last_trace(self):
-        return self.adapter.last_trace
+    stats = property(lambda self: self.adapter.stats)
+    last_trace = property(lambda self: self.adapter.last_trace)
 
     def create_weights(self, *args: Any, **kwargs: Any):
         return self.delegate.create_weights(*args, **kwargs)
@@ -60,101 +127,52 @@ class ZCutlassUnquantizedLinearMethod(LinearMethodBase):  # type: ignore[misc,va
             self.delegate.process_weights_after_loading(layer)
         clear_zcutlass_weight_cache(layer)
 
-    def _delegate_without_transpose_reason(self, layer, x) -> tuple[str, str] | None:
+    def _profit_policy_reject_reason(self, layer, x, m: int, n: int, k: int, family: str) -> Optional[str]:
+        policy = profit_policy()
+        if policy in PASS_THROUGH_POLICIES:
+            return None
+        case = ProfitCase(policy, str(getattr(x, "dtype", "")).lower(), family, getattr(layer, "bias", None) is not None,
+                          str(getattr(layer, "prefix", "")).lower(), (m, n, k))
+        return first_reason(PROFIT_RULES, case)
+
+    def _delegate_without_transpose_reason(self, layer, x) -> Optional[tuple[str, str]]:
+        """(reason, family) when this call goes to vLLM's own GEMM whatever the
+        operands hold: decided from shapes and policy, before any weight copy."""
         if self.adapter.force_zcutlass:
             return None
-        xs = getattr(x, "shape", None)
-        ws = getattr(getattr(layer, "weight", None), "shape", None)
-        if xs is None or ws is None or len(xs) != 2 or len(ws) != 2:
-            return ("rank_not_2", "unknown")
-        m, k = int(xs[0]), int(xs[1])
-        n, weight_k = int(ws[0]), int(ws[1])
-        if k != weight_k:
-            return ("inner_dimension_mismatch", "unknown")
-        family = self.adapter.routing_policy.family(m, n, k)
-        if family == "fallback":
-            return ("shape_not_target_bucket", family)
-        if family not in self.adapter.promoted_families:
-            return ("family_not_promoted", family)
-        reason = self._profit_policy_reject_reason(layer, x, m, n, k, family)
-        return (reason, family) if reason is not None else None
-
-    def _profit_policy_reject_reason(self, layer, x, m: int, n: int, k: int, family: str) -> str | None:
-        """ZCUTLASS_VLLM_PROFIT_POLICY: off/all/experimental route everything the
-        family policy allows; `measured` keeps only the subset the reference
-        measured as profitable (f16 prefill qkv_proj with bias, 256x2048x1536)."""
-        policy = os.environ.get("ZCUTLASS_VLLM_PROFIT_POLICY", "off").strip().lower()
-        if policy in ("", "0", "off", "none", "false", "disabled", "all", "experimental"):
-            return None
-        if policy != "measured":
-            return "profit_policy_unknown"
-        if str(getattr(x, "dtype", "")).lower() not in _HALF_NAMES:
-            return "profit_policy_dtype_not_promoted"
-        if family != "prefill":
-            return "profit_policy_family_not_promoted"
-        if getattr(layer, "bias", None) is None:
-            return "profit_policy_bias_not_promoted"
-        if "qkv_proj" not in str(getattr(layer, "prefix", "")).lower():
-            return "profit_policy_layer_not_promoted"
-        if (m, n, k) == (256, 2048, 1536):
-            return None
-        return "profit_policy_shape_not_promoted"
-
-    def _transposed_weight(self, layer):
-        weight = layer.weight
-        if not self.cache_transposed_weight:
-            self.last_weight_cache = "disabled"
-            return weight.t().contiguous()
-        signature = (int(weight.data_ptr()) if hasattr(weight, "data_ptr") else 0, tuple(weight.shape),
-                     str(weight.dtype), str(weight.device))
-        cached = getattr(layer, "_zcutlass_weight_t_cache", None)
-        if cached is not None and cached[0] == signature:
-            self.last_weight_cache = "hit"
-            return cached[1]
-        weight_t = weight.t().contiguous()
-        setattr(layer, "_zcutlass_weight_t_cache", (signature, weight_t))
-        self.last_weight_cache = "miss"
-        return weight_t
+        shape = LinearShape.of(x, getattr(layer, "weight", None), self.adapter.routing_policy, weight_nk=True)
+        fast = fast_reason(SHAPE_RULES, shape)
+        if fast is not None:
+            return fast
+        reason = self._profit_policy_reject_reason(layer, x, shape.m, shape.n, shape.k, shape.family)
+        return None if reason is None else (reason, shape.family)
 
     def apply(self, layer, x, bias=None):
-        fast = self._delegate_without_transpose_reason(layer, x)
-        if fast is not None:
-            reason, family = fast
+        def vllm_gemm():
+            return self.delegate.apply(layer, x, bias)
+
+        early = self._delegate_without_transpose_reason(layer, x)
+        if early is not None:
             self.last_weight_cache = "skipped"
-            self.adapter._record_fallback_trace(reason=reason, family=family,
-                                                fallback_path_name="vllm_unquantized_fallback")
+            self.adapter.record_delegation(early[0], early[1], FALLBACK_PATH)
+            out = vllm_gemm()
         elif self.native_weight_layout:
             self.last_weight_cache = "native"
-            out = self.adapter.run_native(x, layer.weight, bias,
-                                          fallback_fn=lambda: self.delegate.apply(layer, x, bias),
-                                          fallback_path_name="vllm_unquantized_fallback")
-            self._tag_trace()
-            return out
+            out = self.adapter.run_native(x, layer.weight, bias, fallback_fn=vllm_gemm, fallback_path_name=FALLBACK_PATH)
         else:
-            weight_t = self._transposed_weight(layer)
-            out = self.adapter.run(x, weight_t, bias, weight_is_transposed=True,
-                                   fallback_fn=lambda: self.delegate.apply(layer, x, bias),
-                                   fallback_path_name="vllm_unquantized_fallback")
-            self._tag_trace()
-            return out
-        self._tag_trace()
-        return self.delegate.apply(layer, x, bias)
-
-    def _tag_trace(self) -> None:
+            weight_kn, self.last_weight_cache = transposed_weight(layer, self.cache_transposed_weight)
+            out = self.adapter.run(x, weight_kn, bias, weight_is_transposed=True, fallback_fn=vllm_gemm,
+                                   fallback_path_name=FALLBACK_PATH)
         if self.adapter.last_trace is not None:
             self.adapter.last_trace["weight_cache"] = self.last_weight_cache
-
-
-def clear_zcutlass_weight_cache(layer) -> None:
-    if hasattr(layer, "_zcutlass_weight_t_cache"):
-        delattr(layer, "_zcutlass_weight_t_cache")
+        return out
 
 
 def install_zcutlass_unquantized_linear_method(layer, *, promoted_families: tuple[str, ...] = (),
                                                force_zcutlass: bool = False, materialize_inputs: bool = True,
                                                cache_transposed_weight: bool = True,
                                                native_weight_layout: bool = False) -> ZCutlassUnquantizedLinearMethod:
-    """Replaces one vLLM Linear layer's unquantized method with the zcutlass wrapper."""
+    """Wraps one vLLM Linear layer's UnquantizedLinearMethod (idempotent)."""
     if UnquantizedLinearMethod is None:
         raise ImportError("vLLM is required to install ZCutlassUnquantizedLinearMethod")
     current = getattr(layer, "quant_method", None)
@@ -162,9 +180,8 @@ def install_zcutlass_unquantized_linear_method(layer, *, promoted_families: tupl
         return current
     if current is not None and not isinstance(current, UnquantizedLinearMethod):
         raise TypeError("zcutlass can only wrap vLLM UnquantizedLinearMethod layers in v1.5")
-    method = ZCutlassUnquantizedLinearMethod(current, promoted_families=promoted_families,
-                                             force_zcutlass=force_zcutlass, materialize_inputs=materialize_inputs,
-                                             cache_transposed_weight=cache_transposed_weight,
-                                             native_weight_layout=native_weight_layout)
-    layer.quant_method = method
-    return method
+    layer.quant_method = ZCutlassUnquantizedLinearMethod(
+        current, promoted_families=promoted_families, force_zcutlass=force_zcutlass,
+        materialize_inputs=materialize_inputs, cache_transposed_weight=cache_transposed_weight,
+        native_weight_layout=native_weight_layout)
+    return layer.quant_method
