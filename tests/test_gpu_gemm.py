@@ -68,6 +68,8 @@ FAMILIES = {
     "sk32": "_32x128x64_swapab_streamk",
     "sk64": "_64x128x64_swapab_streamk",
     "generic": "_generic",
+    "splitk256": "_128x256x64_splitk_cluster",
+    "splitk128": "_128x128x64_splitk_cluster",
 }
 
 # (m, n, k) per family: ragged edges in every dimension, K tails, multi-tile.
@@ -84,6 +86,9 @@ FAMILY_SHAPES = {
     "sk16": [(1, 128, 8192), (7, 300, 200), (16, 1000, 4096), (13, 7168, 1032), (16, 8192, 1024)],
     "sk32": [(17, 128, 128), (32, 520, 777), (25, 2048, 8192)],
     "sk64": [(33, 256, 256), (64, 1000, 1000), (48, 4096, 1536)],
+    # cluster split-K: one tile, ragged edges, the cfg0 shape, several tile rows
+    "splitk256": [(128, 256, 64), (300, 520, 200), (256, 4096, 4096), (1000, 777, 1032)],
+    "splitk128": [(129, 136, 72), (513, 1000, 520), (256, 2048, 1536)],
     # odd leading dimensions (pads 3/5/7/11) on several 128 x 128 tiles, K tails of 1..31
     "generic": [(5, 7, 9), (100, 200, 50), (130, 70, 300), (1000, 777, 1032), (257, 1300, 2101)],
 }
@@ -127,6 +132,22 @@ def test_forced_family(cuda_device, monkeypatch, fam, shape, dt, col):
         sel = selected(c)
         assert FAMILIES[fam] in sel["kernel_name"], sel
         check_case(c)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("splits", [1, 2, 3, 5, 8])
+@pytest.mark.parametrize("bn", [128, 256])
+def test_splitk_split_counts(cuda_device, monkeypatch, splits, bn):
+    """Every cluster size the split-K kernel can get, on a ragged problem whose
+    K blocks do not divide evenly (17 blocks of 64, the last one partial)."""
+    monkeypatch.setenv("ZCUTLASS_FORCE_KERNEL", f"_128x{bn}x64_splitk_cluster")
+    monkeypatch.setenv("ZCUTLASS_SPLITK", str(splits))
+    for dt in (F16, BF16):
+        for i, (alpha, beta, bias) in enumerate(EPILOGUES):
+            c = Case(f"splitk{bn} s{splits} {i}", dt, 200, 600, 1080, alpha, beta, bias, 0, 0, 0, 8,
+                     b_col_major=(i % 2 == 1), gen="normal", seed=splits * 10 + i)
+            assert FAMILIES[f"splitk{bn}"] in selected(c)["kernel_name"]
+            check_case(c)
 
 
 # ---------------------------------------------------------------- config shapes

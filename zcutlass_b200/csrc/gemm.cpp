@@ -8,7 +8,7 @@
 //   gemm()             gemm.cu:609-629  (zero-size -> Success without writes)
 //   selected_kernel_*  gemm.cu:631-688  (host-only, dummy non-null pointers)
 //   can_implement / get_workspace_size / version  gemm.cu:695-756
-// The operation table itself is new: three sm_100a kernel families plus a
+// The operation table itself is new: four sm_100a kernel families plus a
 // predicated CUDA-core kernel for layouts TMA cannot express.
 #include "zcutlass/gemm.hpp"
 
@@ -127,7 +127,7 @@ SelectDevice select_device() {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-enum class Kind { UmmaPair, UmmaPersistent, UmmaSwapAb, UmmaSwapAbStreamK, Generic };
+enum class Kind { UmmaPair, UmmaPersistent, UmmaSplitK, UmmaSwapAb, UmmaSwapAbStreamK, Generic };
 
 class Sm100Operation final : public GemmOperation {
  public:
@@ -189,15 +189,22 @@ class Sm100Operation final : public GemmOperation {
       // (listed first) takes the shapes where split-K would idle SMs.
       return kind_ == Kind::UmmaSwapAb || zcb::swapab_prefer_streamk(n, k, dev.sm_count);
     }
-    // Persistent kernel: D goes out through TMA; C and bias are read with
-    // 16-byte vector loads.
+    // Persistent and split-K kernels: D goes out through TMA or aligned vector
+    // stores; C and bias are read with vector loads.
     if (!zcb::tma_compatible(args.D.data, args.D.ld)) return false;
     if (args.beta != 0.0f && (!aligned16(args.C.data) || (args.C.ld & 7) != 0)) return false;
     if (args.bias != nullptr && !aligned16(args.bias)) return false;
     if (forced) return true;
-    const zcb::PersistentConfig want = zcb::choose_persistent(m, n, dev.sm_count);
-    if (kind_ == Kind::UmmaPair) return want == zcb::PersistentConfig::Pair256x256;
-    return want == (desc_.tile_n == 256 ? zcb::PersistentConfig::Cta128x256 : zcb::PersistentConfig::Cta128x128);
+    using PC = zcb::PersistentConfig;
+    const PC want = zcb::choose_tiles(m, n, k, dev.sm_count).config;
+    switch (kind_) {
+      case Kind::UmmaPair:
+        return want == PC::Pair256x256;
+      case Kind::UmmaSplitK:
+        return want == (desc_.tile_n == 256 ? PC::SplitK128x256 : PC::SplitK128x128);
+      default:
+        return want == (desc_.tile_n == 256 ? PC::Cta128x256 : PC::Cta128x128);
+    }
   }
 
   Status run(const GemmArguments& args, const GemmPreference&) const override {
@@ -227,6 +234,16 @@ class Sm100Operation final : public GemmOperation {
       case Kind::UmmaPersistent:
         e = zcb::launch_umma_gemm(la, desc_.tile_n);
         break;
+      case Kind::UmmaSplitK: {
+        const SelectDevice dev = select_device();
+        const zcb::TileChoice tc = zcb::choose_tiles(la.m, la.n, la.k, dev.sm_count);
+        const bool chosen = tc.config == (desc_.tile_n == 256 ? zcb::PersistentConfig::SplitK128x256
+                                                              : zcb::PersistentConfig::SplitK128x128);
+        const int splits = chosen ? tc.splits
+                                  : zcb::splitk_default_splits(la.m, la.n, la.k, desc_.tile_n, dev.sm_count);
+        e = zcb::launch_umma_splitk_gemm(la, desc_.tile_n, splits);
+        break;
+      }
       case Kind::UmmaSwapAbStreamK:
         e = zcb::launch_umma_swapab_sk_gemm(la);
         break;
@@ -252,10 +269,11 @@ void register_builtin_operations() {
   using K = Kind;
   using F = ShapeFamily;
   using E = EpilogueKind;
-  // First match wins: small-M swap-AB buckets, then the persistent kernels
-  // (CTA-pair 256x256, or one-CTA 128x256 / 128x128 tiles, whichever the
-  // wave-quantisation model in choose_persistent picks), then the predicated
-  // CUDA-core kernel that accepts any layout.
+  // First match wins: small-M swap-AB buckets, then the cluster split-K and
+  // persistent kernels (split-K 128x256 / 128x128, CTA-pair 256x256, or
+  // one-CTA 128x256 / 128x128 tiles, whichever the cost model in
+  // choose_tiles picks), then the predicated CUDA-core kernel that accepts
+  // any layout.
   static const Sm100Operation ops[] = {
       {"zcutlass_sm100_tcgen05_bf16_16x128x64_swapab_streamk", DType::BF16, K::UmmaSwapAbStreamK, 16, 128, 64, 12, F::Decode, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_f16_16x128x64_swapab_streamk", DType::F16, K::UmmaSwapAbStreamK, 16, 128, 64, 12, F::Decode, E::RegisterLinear},
@@ -269,6 +287,10 @@ void register_builtin_operations() {
       {"zcutlass_sm100_tcgen05_f16_32x128x64_swapab_splitk", DType::F16, K::UmmaSwapAb, 32, 128, 64, 9, F::Decode, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_bf16_64x128x64_swapab_splitk", DType::BF16, K::UmmaSwapAb, 64, 128, 64, 7, F::Prefill, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_f16_64x128x64_swapab_splitk", DType::F16, K::UmmaSwapAb, 64, 128, 64, 7, F::Prefill, E::RegisterLinear},
+      {"zcutlass_sm100_tcgen05_bf16_128x256x64_splitk_cluster", DType::BF16, K::UmmaSplitK, 128, 256, 64, 4, F::Prefill, E::RegisterLinear},
+      {"zcutlass_sm100_tcgen05_f16_128x256x64_splitk_cluster", DType::F16, K::UmmaSplitK, 128, 256, 64, 4, F::Prefill, E::RegisterLinear},
+      {"zcutlass_sm100_tcgen05_bf16_128x128x64_splitk_cluster", DType::BF16, K::UmmaSplitK, 128, 128, 64, 6, F::Prefill, E::RegisterLinear},
+      {"zcutlass_sm100_tcgen05_f16_128x128x64_splitk_cluster", DType::F16, K::UmmaSplitK, 128, 128, 64, 6, F::Prefill, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_bf16_256x256x64_2cta_persistent", DType::BF16, K::UmmaPair, 256, 256, 64, 6, F::Large, E::TmemRegisterTma},
       {"zcutlass_sm100_tcgen05_f16_256x256x64_2cta_persistent", DType::F16, K::UmmaPair, 256, 256, 64, 6, F::Large, E::TmemRegisterTma},
       {"zcutlass_sm100_tcgen05_bf16_128x256x64_ws_persistent", DType::BF16, K::UmmaPersistent, 128, 256, 64, 4, F::Large, E::TmemRegisterTma},

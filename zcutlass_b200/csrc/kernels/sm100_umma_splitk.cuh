@@ -1,0 +1,320 @@
+// Cluster split-K tcgen05 GEMM for sm_100a: mid-size problems whose output
+// has too few 128 x BN tiles to occupy every SM (M of a few hundred tokens,
+// e.g. 256 x 4096 x 4096 has 32 tiles of 128 x 256 for 148 SMs).
+//
+//   D[M,N] = alpha * A[M,K] * B[K,N] + beta * C[M,N] + bias[N]     (row-major, f16/bf16)
+//
+// One thread-block cluster of S CTAs computes one 128 x BN output tile; CTA r
+// of the cluster runs K blocks [r*KB/S, (r+1)*KB/S) through the same
+// warp-specialised pipeline as the persistent kernel (warp 0 TMA producer,
+// warp 1 MMA issuer with a BN-column TMEM accumulator, warps 2-5 epilogue).
+// Afterwards:
+//   1. the epilogue warps copy the FP32 partial tile from TMEM into this CTA's
+//      shared memory ([128][BN + 4] floats, over the drained pipeline ring);
+//   2. cluster barrier: every partial is in place;
+//   3. CTA r owns rows [r*128/S, (r+1)*128/S) of the tile: each thread reads a
+//      4-column group of its rows from every CTA's partial through distributed
+//      shared memory (ld.shared::cluster.v4), adds them in CTA order -- the
+//      sum does not depend on timing -- applies alpha/beta/bias, rounds once
+//      and stores 4 outputs (8 bytes) to D;
+//   4. cluster barrier: no CTA leaves while a peer still reads its partial.
+// No global scratch memory is used. Ragged M/N/K: TMA zero-fills loads
+// outside A and B; rows and columns outside D are never stored.
+#pragma once
+
+#include "sm100_ptx.cuh"
+#include "sm100_umma_gemm.cuh"  // kEpiHasC / kEpiHasBias
+
+namespace zcb {
+
+struct SplitKParams {
+  int m, n, k;
+  int num_kb;  // K blocks of 64
+  int splits;  // CTAs per cluster, along K
+  float alpha, beta;
+  const void* c;
+  int64_t ldc;
+  const void* bias;
+  void* d;
+  int64_t ldd;
+  uint32_t epi_flags;
+  int* error_word;
+};
+
+namespace splitk {
+
+constexpr int kBlockM = 128;
+constexpr int kBlockK = 64;
+constexpr int kUmmaK = 16;
+constexpr int kThreads = 192;
+constexpr int kEpiWarps = 4;
+constexpr int kMaxSplits = 8;  // portable cluster size
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr int kABytes = kBlockM * kBlockK * 2;     // 16 KiB
+  static constexpr int kBChunkBytes = kBlockK * 128;        // 64(n) x 64(k) box: 8 KiB
+  static constexpr int kBBytes = (BN / 64) * kBChunkBytes;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kAOff = 0;
+  static constexpr int kBOff = STAGES * kABytes;
+  static constexpr int kRingBytes = STAGES * kStageBytes;
+  // FP32 partial, row stride BN + 4 floats: the TMEM-to-shared copy (a row
+  // per thread, 16-byte stores) is free of bank conflicts.
+  static constexpr int kRedStride = BN + 4;
+  static constexpr int kRedBytes = kBlockM * kRedStride * 4;
+  static constexpr int kBarOff = kRingBytes;
+  static constexpr int kNumBars = 2 * STAGES + 2;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+  static constexpr int kBytes = kMiscOff + 16;
+  static constexpr int kDynamicBytes = kBytes + 1024;
+  static_assert(BN == 128 || BN == 256, "BN must be 128 or 256");
+  static_assert(kRedBytes <= kRingBytes, "the partial tile must fit in the drained pipeline ring");
+  static_assert(kDynamicBytes <= 232448, "shared memory budget exceeded");
+};
+
+enum : int {
+  kErrProducerEmpty = (20 << 4) | 1,
+  kErrMmaFull = (21 << 4) | 2,
+  kErrEpiTmemFull = (22 << 4) | 3,
+};
+
+__device__ __forceinline__ float4 ld_dsmem_v4(uint32_t local_addr, uint32_t rank) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(map_shared_rank(local_addr, rank))
+               : "memory");
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ float4 load4(const T* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);  // 8-byte aligned by the launch contract
+  const float2 lo = Elem<T>::unpack(u.x), hi = Elem<T>::unpack(u.y);
+  return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+
+// kBKMajor: B is column-major (a PyTorch [N, K] weight): its tiles are K-major.
+template <typename T, int BN, int STAGES, bool kBKMajor>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                const SplitKParams p) {
+  using L = Smem<BN, STAGES>;
+  constexpr uint32_t kTmemCols = BN;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tmem_full = empty + STAGES;
+  uint64_t* drain = tmem_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOff + 4);
+  float* red = reinterpret_cast<float*>(smem);  // over the ring, once the main loop is done
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // the cluster spans gridDim.x == p.splits
+  const int n0 = blockIdx.y * BN;
+  const int m0 = blockIdx.z * kBlockM;
+  const int kb_begin = static_cast<int>((static_cast<int64_t>(rank) * p.num_kb) / p.splits);
+  const int kb_end = static_cast<int>((static_cast<int64_t>(rank + 1) * p.num_kb) / p.splits);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tmem_full, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // inputs/outputs may belong to the previous kernel on the stream
+  griddep_launch_dependents();
+  const WaitCtx ctx{abort_flag, p.error_word};
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
+        const uint32_t s = it % STAGES;
+        if (!mbar_wait(&empty[s], ((it / STAGES) & 1u) ^ 1u, ctx, kErrProducerEmpty)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+        tma_load_2d(smem + L::kAOff + s * L::kABytes, &tmap_a, &full[s], kb * kBlockK, m0);
+        if constexpr (kBKMajor) {
+          tma_load_2d(smem + L::kBOff + s * L::kBBytes, &tmap_b, &full[s], kb * kBlockK, n0);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j)
+            tma_load_2d(smem + L::kBOff + s * L::kBBytes + j * L::kBChunkBytes, &tmap_b, &full[s], n0 + 64 * j,
+                        kb * kBlockK);
+        }
+      }
+      if (!ok) {
+        const uint32_t first = it > static_cast<uint32_t>(STAGES) ? it - STAGES : 0u;
+        for (uint32_t j = first; j < it; ++j) mbar_wait_quiet(&full[j % STAGES], (j / STAGES) & 1u, 200000000ull);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t kIdesc = umma_idesc_f16<Elem<T>::kBf16>(kBlockM, BN, false, !kBKMajor);
+      uint32_t it = 0;
+      bool ok = true, issued = false;
+      for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
+        const uint32_t s = it % STAGES;
+        if (!mbar_wait(&full[s], (it / STAGES) & 1u, ctx, kErrMmaFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after_sync();
+        const uint32_t a_addr = smem_addr(smem + L::kAOff + s * L::kABytes);
+        const uint32_t b_addr = smem_addr(smem + L::kBOff + s * L::kBBytes);
+#pragma unroll
+        for (int kk = 0; kk < kBlockK / kUmmaK; ++kk) {
+          const uint64_t a_desc = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+          const uint64_t b_desc = kBKMajor ? smem_desc_sw128(b_addr + kk * 32, 16, 1024)
+                                           : smem_desc_sw128(b_addr + kk * 2048, L::kBChunkBytes, 1024);
+          umma_f16_ss(tmem_base, a_desc, b_desc, kIdesc, (it | kk) != 0 ? 1u : 0u);
+        }
+        issued = true;
+        umma_commit(&empty[s]);
+      }
+      if (ok && issued) {
+        umma_commit(tmem_full);
+      } else if (ok) {
+        mbar_arrive(tmem_full);  // no K blocks for this CTA: its partial is zero
+      } else if (issued) {
+        umma_commit(drain);
+        mbar_wait_quiet(drain, 0, 200000000ull);
+      }
+    }
+    __syncwarp();
+  } else {
+    // Partial tile from TMEM to shared memory: thread = row of the tile.
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const bool ok = mbar_wait(tmem_full, 0, ctx, kErrEpiTmemFull);
+    if (__all_sync(0xffffffffu, ok)) {
+      tc_fence_after_sync();
+      float4* dst = reinterpret_cast<float4*>(red + row * L::kRedStride);
+      if (kb_end > kb_begin) {
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t acc[32];
+          tmem_ld_32x32b_x32(taddr + c * 32, acc);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            dst[c * 8 + j] = make_float4(__uint_as_float(acc[4 * j]), __uint_as_float(acc[4 * j + 1]),
+                                         __uint_as_float(acc[4 * j + 2]), __uint_as_float(acc[4 * j + 3]));
+        }
+      } else {
+#pragma unroll 4
+        for (int j = 0; j < BN / 4; ++j) dst[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  }
+
+  // Every thread of every CTA reaches both cluster barriers, on the abort
+  // path too, so no CTA waits for a peer that left.
+  tc_fence_before_sync();
+  __syncwarp();
+  cluster_sync_all();
+
+  if (*abort_flag == 0) {  // an aborted CTA has no partial; its error code is already recorded
+    const T* cptr = static_cast<const T*>(p.c);
+    const T* bptr = static_cast<const T*>(p.bias);
+    T* dptr = static_cast<T*>(p.d);
+    const bool has_c = (p.epi_flags & kEpiHasC) != 0;
+    const bool has_bias = (p.epi_flags & kEpiHasBias) != 0;
+    const int r_begin = static_cast<int>((rank * kBlockM) / p.splits);
+    const int r_end = static_cast<int>(((rank + 1) * kBlockM) / p.splits);
+    constexpr int kGroups = BN / 4;  // 4-column groups per row
+    const int total = (r_end - r_begin) * kGroups;
+    const uint32_t red_addr = smem_addr(red);
+#pragma unroll 1
+    for (int g = threadIdx.x; g < total; g += kThreads) {
+      const int rl = r_begin + g / kGroups;
+      const int cl = (g % kGroups) * 4;
+      const int row = m0 + rl, col = n0 + cl;
+      if (row >= p.m || col >= p.n) continue;
+      const uint32_t off = static_cast<uint32_t>((rl * L::kRedStride + cl) * 4);
+      float4 part[kMaxSplits];  // every remote load first: one DSMEM round trip
+#pragma unroll
+      for (int s = 0; s < kMaxSplits; ++s)
+        if (s < p.splits) part[s] = ld_dsmem_v4(red_addr + off, static_cast<uint32_t>(s));
+      float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int s = 0; s < kMaxSplits; ++s) {
+        if (s < p.splits) {
+          sum.x += part[s].x;
+          sum.y += part[s].y;
+          sum.z += part[s].z;
+          sum.w += part[s].w;
+        }
+      }
+      float v[4] = {p.alpha * sum.x, p.alpha * sum.y, p.alpha * sum.z, p.alpha * sum.w};
+      const int valid = p.n - col < 4 ? p.n - col : 4;
+      if (valid == 4) {
+        if (has_c) {
+          const float4 cv = load4(cptr + static_cast<int64_t>(row) * p.ldc + col);
+          v[0] += p.beta * cv.x;
+          v[1] += p.beta * cv.y;
+          v[2] += p.beta * cv.z;
+          v[3] += p.beta * cv.w;
+        }
+        if (has_bias) {
+          const float4 bv = load4(bptr + col);
+          v[0] += bv.x;
+          v[1] += bv.y;
+          v[2] += bv.z;
+          v[3] += bv.w;
+        }
+        uint2 out;
+        out.x = Elem<T>::pack(v[0], v[1]);
+        out.y = Elem<T>::pack(v[2], v[3]);
+        *reinterpret_cast<uint2*>(dptr + static_cast<int64_t>(row) * p.ldd + col) = out;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (j < valid) {
+            float x = v[j];
+            if (has_c) x += p.beta * Elem<T>::to_float(cptr[static_cast<int64_t>(row) * p.ldc + col + j]);
+            if (has_bias) x += Elem<T>::to_float(bptr[col + j]);
+            dptr[static_cast<int64_t>(row) * p.ldd + col + j] = Elem<T>::from_float(x);
+          }
+        }
+      }
+    }
+  }
+
+  __syncwarp();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace splitk
+}  // namespace zcb

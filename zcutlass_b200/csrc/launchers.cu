@@ -10,6 +10,7 @@
 #include "kernels/sm100_umma_gemm.cuh"
 #include "kernels/sm100_umma_gemm_2cta.cuh"
 #include "kernels/sm100_umma_swapab.cuh"
+#include "kernels/sm100_umma_splitk.cuh"
 #include "kernels/sm100_umma_swapab_sk.cuh"
 #include "tma_desc.hpp"
 
@@ -39,6 +40,8 @@ struct DeviceSlot {
   std::atomic<uint64_t> attr_done{0};
   // Resident CTA pairs of each cluster-launched configuration (0 = not queried).
   int max_active_pairs[64] = {};
+  // Resident clusters of each split-K configuration by cluster size (0 = not queried).
+  int max_active_clusters[64][9] = {};
 };
 DeviceSlot g_devices[kMaxDevices];
 
@@ -282,6 +285,76 @@ cudaError_t launch_umma2_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit
   return cudaGetLastError();
 }
 
+template <typename T, int BN, int STAGES, bool KM>
+cudaError_t launch_splitk_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit, int splits) {
+  using L = splitk::Smem<BN, STAGES>;
+  CUtensorMap ta, tb;
+  const bool bf16 = a.bf16;
+  const bool b_ok = KM ? make_tma_2d(&tb, a.b, bf16, a.n, a.k, a.ldb, BN, splitk::kBlockK, TmaSwizzle::B128)
+                       : make_tma_2d(&tb, a.b, bf16, a.k, a.n, a.ldb, splitk::kBlockK, 64, TmaSwizzle::B128);
+  if (!b_ok || !make_tma_2d(&ta, a.a, bf16, a.m, a.k, a.lda, splitk::kBlockM, splitk::kBlockK, TmaSwizzle::B128))
+    return cudaErrorInvalidValue;
+  const int64_t tiles_m = (a.m + splitk::kBlockM - 1) / splitk::kBlockM;
+  const int64_t tiles_n = (a.n + BN - 1) / BN;
+  if (tiles_m > 65535 || tiles_n > 65535) return cudaErrorInvalidValue;
+  SplitKParams p{};
+  p.m = static_cast<int>(a.m);
+  p.n = static_cast<int>(a.n);
+  p.k = static_cast<int>(a.k);
+  p.num_kb = static_cast<int>((a.k + splitk::kBlockK - 1) / splitk::kBlockK);
+  p.alpha = a.alpha;
+  p.beta = a.beta;
+  p.c = a.c;
+  p.ldc = a.ldc;
+  p.bias = a.bias;
+  p.d = a.d;
+  p.ldd = a.ldd;
+  p.epi_flags = (a.beta != 0.0f ? kEpiHasC : 0u) | (a.bias != nullptr ? kEpiHasBias : 0u);
+  p.error_word = slot->info.error_word;
+
+  auto kernel = splitk::gemm_kernel<T, BN, STAGES, KM>;
+  cudaError_t e = ensure_smem_attr(slot, config_bit, kernel, L::kDynamicBytes);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(splitk::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = L::kDynamicBytes;
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;  // the occupancy query sees the cluster shape only
+  // The whole grid should be resident at once (every cluster is one wave of
+  // work): fewer CTAs per cluster when that many clusters of `splits` CTAs
+  // cannot be co-resident (a cluster must fit in one GPC).
+  splits = std::max(1, std::min(std::min(splits, splitk::kMaxSplits), p.num_kb));
+  for (; splits > 1; --splits) {
+    int& active = slot->max_active_clusters[config_bit][splits];
+    if (active == 0) {
+      attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+      cfg.gridDim = dim3(static_cast<unsigned>(splits), static_cast<unsigned>(tiles_n), static_cast<unsigned>(tiles_m));
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters <= 0) {
+        (void)cudaGetLastError();
+        clusters = -1;  // unknown: do not trust this cluster size
+      }
+      active = clusters;
+    }
+    if (active >= tiles_m * tiles_n) break;
+  }
+  p.splits = splits;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+  cfg.gridDim = dim3(static_cast<unsigned>(splits), static_cast<unsigned>(tiles_n), static_cast<unsigned>(tiles_m));
+  unsigned int nattr = 1;
+  add_pdl_attr(attr, nattr);
+  cfg.numAttrs = nattr;
+  e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, p);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
 // Stream-K workspace, one per (device, stream): tile counters followed by the
 // FP32 partial slots. Kernels on one stream run in order, so they can share
 // it; kernels on different streams may overlap, so they never do. Grown on
@@ -439,6 +512,10 @@ enum : int {
   kCfgGatherUmmaF16N256,
   kCfgGatherUmmaBf16N128,
   kCfgGatherUmmaF16N128,
+  kCfgSplitKBf16N256,
+  kCfgSplitKF16N256,
+  kCfgSplitKBf16N128,
+  kCfgSplitKF16N128,
   kCfgColMajorB = 32,
 };
 
@@ -469,6 +546,17 @@ cudaError_t launch_umma_km(const LaunchArgs& a, DeviceSlot* slot, int bn) {
 }
 
 template <bool KM>
+cudaError_t launch_splitk_km(const LaunchArgs& a, DeviceSlot* slot, int bn, int splits) {
+  const int off = KM ? kCfgColMajorB : 0;
+  if (bn == 256) {
+    return a.bf16 ? launch_splitk_t<__nv_bfloat16, 256, 4, KM>(a, slot, kCfgSplitKBf16N256 + off, splits)
+                  : launch_splitk_t<half, 256, 4, KM>(a, slot, kCfgSplitKF16N256 + off, splits);
+  }
+  return a.bf16 ? launch_splitk_t<__nv_bfloat16, 128, 6, KM>(a, slot, kCfgSplitKBf16N128 + off, splits)
+                : launch_splitk_t<half, 128, 6, KM>(a, slot, kCfgSplitKF16N128 + off, splits);
+}
+
+template <bool KM>
 cudaError_t launch_swapab_km(const LaunchArgs& a, DeviceSlot* slot, int splits) {
   const int off = KM ? kCfgColMajorB : 0;
   if (a.m <= 16) {
@@ -488,6 +576,52 @@ cudaError_t launch_swapab_km(const LaunchArgs& a, DeviceSlot* slot, int splits) 
 const DeviceInfo* current_device_info() {
   DeviceSlot* slot = current_slot();
   return slot ? &slot->info : nullptr;
+}
+
+TileChoice choose_tiles(int64_t m, int64_t n, int64_t k, int sm_count) {
+  // Persistent configurations: waves x tile area / efficiency, as in
+  // choose_persistent, times the full K. Split-K configurations (one wave of
+  // tiles x S clusters' CTAs): tile area x (K/S + the reduction, costed as two
+  // K blocks) / the same efficiency. Split-K only competes when the tiles
+  // alone fill at most half the SMs.
+  const int64_t kb = (k + 63) / 64;
+  const PersistentConfig base = choose_persistent(m, n, sm_count);
+  const auto persistent_cost = [&](PersistentConfig c) {
+    const int tm = c == PersistentConfig::Pair256x256 ? 256 : 128;
+    const int tn = c == PersistentConfig::Cta128x128 ? 128 : 256;
+    const int units = c == PersistentConfig::Pair256x256 ? sm_count / 2 : sm_count;
+    const double area = c == PersistentConfig::Pair256x256 ? 256.0 * 256.0 / 2.0 : double(tm) * tn;
+    const double eff = c == PersistentConfig::Pair256x256 ? 1.0 : c == PersistentConfig::Cta128x256 ? 0.86 : 0.72;
+    const int64_t tiles = ((m + tm - 1) / tm) * ((n + tn - 1) / tn);
+    return double((tiles + units - 1) / units) * area * double(kb) / eff;
+  };
+  TileChoice best{base, 1};
+  double best_cost = persistent_cost(base);
+  const char* forced = std::getenv("ZCUTLASS_SPLITK");
+  const int forced_splits = forced != nullptr ? std::atoi(forced) : 0;
+  for (const int bn : {256, 128}) {
+    const int64_t tiles = ((m + 127) / 128) * ((n + bn - 1) / bn);
+    if (tiles <= 0 || tiles * 2 > sm_count || kb <= 0) continue;
+    int64_t s = std::min<int64_t>({int64_t(splitk::kMaxSplits), sm_count / tiles, kb / 2});
+    if (forced_splits > 0) s = std::min<int64_t>(std::min<int64_t>(forced_splits, splitk::kMaxSplits), kb);
+    if (s < 2) continue;
+    const double eff = bn == 256 ? 0.86 : 0.72;
+    const double cost = 128.0 * bn * (double((kb + s - 1) / s) + 2.0) / eff;
+    if (cost < best_cost * 0.999) {
+      best_cost = cost;
+      best = {bn == 256 ? PersistentConfig::SplitK128x256 : PersistentConfig::SplitK128x128, static_cast<int>(s)};
+    }
+  }
+  return best;
+}
+
+int splitk_default_splits(int64_t m, int64_t n, int64_t k, int bn, int sm_count) {
+  const int64_t kb = (k + 63) / 64;
+  const int64_t tiles = std::max<int64_t>(1, ((m + 127) / 128) * ((n + bn - 1) / bn));
+  const char* forced = std::getenv("ZCUTLASS_SPLITK");
+  int64_t s = forced != nullptr && std::atoi(forced) > 0 ? std::atoi(forced) : sm_count / tiles;
+  s = std::min<int64_t>({s, int64_t(splitk::kMaxSplits), kb});
+  return static_cast<int>(std::max<int64_t>(s, 1));
 }
 
 PersistentConfig choose_persistent(int64_t m, int64_t n, int sm_count) {
@@ -542,6 +676,12 @@ cudaError_t launch_umma_gemm(const LaunchArgs& a, int bn) {
                   : launch_umma_t<half, 128, 6, true, kMaxAParts>(a, slot, kCfgGatherUmmaF16N128);
   }
   return a.b_col_major ? launch_umma_km<true>(a, slot, bn) : launch_umma_km<false>(a, slot, bn);
+}
+
+cudaError_t launch_umma_splitk_gemm(const LaunchArgs& a, int bn, int splits) {
+  DeviceSlot* slot = current_slot();
+  if (slot == nullptr) return cudaErrorInvalidDevice;
+  return a.b_col_major ? launch_splitk_km<true>(a, slot, bn, splits) : launch_splitk_km<false>(a, slot, bn, splits);
 }
 
 cudaError_t launch_umma_pair_gemm(const LaunchArgs& a) {
