@@ -59,6 +59,7 @@ struct Options {
   int warmup = 10, iterations = 50, rotate = 1;
   float alpha = 1.0f, beta = 0.0f;
   bool bias = false, json = false, append = false, experimental = false;
+  bool graph = false;
 };
 
 struct Shape {
@@ -71,7 +72,9 @@ void usage() {
                "  [--providers zcutlass,cublas] [--json] [--output FILE] [--append]\n"
                "  [--warmup N] [--iterations N] [--alpha X] [--beta X] [--bias]\n"
                "  [--b-layout row|col] [--rotate R] [--force-kernel SUBSTR]\n"
-               "  [--experimental-kernels] [--experimental-kernel NAME]\n";
+               "  [--experimental-kernels] [--experimental-kernel NAME] [--graph]\n"
+               "  --graph: capture the timed launches in one CUDA graph and report the\n"
+               "           device time per launch (no host launch latency in the figure)\n";
 }
 
 Options parse(int argc, char** argv) {
@@ -102,6 +105,7 @@ Options parse(int argc, char** argv) {
     else if (a == "--rotate") o.rotate = std::max(1, std::atoi(val()));
     else if (a == "--force-kernel") o.force_kernel = val();
     else if (a == "--json") o.json = true;
+    else if (a == "--graph") o.graph = true;
     else if (a == "--experimental-kernels") o.experimental = true;
     else if (a == "--experimental-kernel") {
       o.experimental = true;
@@ -204,6 +208,38 @@ float time_ms(Fn&& fn, int warmup, int iterations) {
   return samples[samples.size() / 2];
 }
 
+// Device time per launch: `iterations` calls captured once in a CUDA graph on
+// `stream` (programmatic dependent launch between them as in a serving
+// graph), replayed, and divided by the count. The reference's per-launch
+// event timing above also counts the host's launch latency.
+template <typename Fn>
+float time_graph_ms(Fn&& fn, int warmup, int iterations, cudaStream_t stream) {
+  for (int i = 0; i < warmup; ++i) fn(i);
+  CHECK_CUDA(cudaStreamSynchronize(stream));
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  CHECK_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+  for (int i = 0; i < iterations; ++i) fn(i);
+  CHECK_CUDA(cudaStreamEndCapture(stream, &graph));
+  CHECK_CUDA(cudaGraphInstantiate(&exec, graph, 0));
+  CHECK_CUDA(cudaGraphLaunch(exec, stream));
+  CHECK_CUDA(cudaStreamSynchronize(stream));
+  cudaEvent_t start, stop;
+  CHECK_CUDA(cudaEventCreate(&start));
+  CHECK_CUDA(cudaEventCreate(&stop));
+  CHECK_CUDA(cudaEventRecord(start, stream));
+  CHECK_CUDA(cudaGraphLaunch(exec, stream));
+  CHECK_CUDA(cudaEventRecord(stop, stream));
+  CHECK_CUDA(cudaEventSynchronize(stop));
+  float ms = 0.0f;
+  CHECK_CUDA(cudaEventElapsedTime(&ms, start, stop));
+  CHECK_CUDA(cudaEventDestroy(start));
+  CHECK_CUDA(cudaEventDestroy(stop));
+  CHECK_CUDA(cudaGraphExecDestroy(exec));
+  CHECK_CUDA(cudaGraphDestroy(graph));
+  return ms / iterations;
+}
+
 double algorithmic_bytes(const Shape& s, const Options& o) {
   return 2.0 * (double(s.m) * s.k + double(s.k) * s.n + double(s.m) * s.n) +
          (o.beta != 0.0f ? 2.0 * double(s.m) * s.n : 0.0) + (o.bias ? 2.0 * s.n : 0.0);
@@ -230,7 +266,8 @@ void emit_record(std::ostream& out, const Options& o, const Shape& s, const char
       << ",\"beta\":" << o.beta << ",\"bias\":" << (o.bias ? "true" : "false") << "}"
       << ",\"provider\":\"" << provider << "\",\"status\":\"success\",\"kernel\":\"" << kernel << "\""
       << ",\"performance\":{\"warmup_iterations\":" << o.warmup << ",\"profiling_iterations\":" << o.iterations
-      << ",\"median_ms\":" << ms << ",\"tflops\":" << tf << ",\"gbps\":" << gbs << ",\"rotate\":" << o.rotate << "}"
+      << ",\"median_ms\":" << ms << ",\"tflops\":" << tf << ",\"gbps\":" << gbs << ",\"rotate\":" << o.rotate
+      << ",\"timing\":\"" << (o.graph ? "cuda_graph_mean" : "per_launch_events_median") << "\"}"
       << ",\"environment\":{\"gpu_name\":\"" << prop.name << "\",\"sm\":" << prop.major << prop.minor
       << ",\"zcutlass_version\":\"" << zcutlass::version_major() << "." << zcutlass::version_minor() << "."
       << zcutlass::version_patch() << "\",\"registered_gemm_operations\":"
@@ -268,7 +305,13 @@ void run_shape(const Shape& s, const Options& o, cublasHandle_t handle, const cu
   T* bias = nullptr;
   CHECK_CUDA(cudaMalloc(&bias, size_t(s.n) * sizeof(T)));
   CHECK_CUDA(cudaMemcpy(bias, hbias.data(), size_t(s.n) * sizeof(T), cudaMemcpyHostToDevice));
-  const zcutlass::GemmDesc desc = make_desc(s, o, z_dtype<T>(), o.bias ? bias : nullptr);
+  zcutlass::GemmDesc desc = make_desc(s, o, z_dtype<T>(), o.bias ? bias : nullptr);
+  cudaStream_t stream = nullptr;
+  if (o.graph) {
+    CHECK_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    desc.stream = stream;
+    CHECK_CUBLAS(cublasSetStream(handle, stream));
+  }
 
   auto z_fn = [&](int i) {
     const int r = i % R;
@@ -281,7 +324,7 @@ void run_shape(const Shape& s, const Options& o, cublasHandle_t handle, const cu
   const float alpha = o.alpha, beta = o.beta;
   auto blas_fn = [&](int i) {
     const int r = i % R;
-    if (beta != 0.0f) CHECK_CUDA(cudaMemcpyAsync(D[r], C[r], c_n * sizeof(T), cudaMemcpyDeviceToDevice));
+    if (beta != 0.0f) CHECK_CUDA(cudaMemcpyAsync(D[r], C[r], c_n * sizeof(T), cudaMemcpyDeviceToDevice, stream));
     // Row-major D = A * B is column-major D^T = B^T * A^T.
     CHECK_CUBLAS(cublasGemmEx(handle, col ? CUBLAS_OP_T : CUBLAS_OP_N, CUBLAS_OP_N, int(s.n), int(s.m), int(s.k),
                               &alpha, B[r], cuda_type<T>(), int(ldb), A[r], cuda_type<T>(), int(lda), &beta,
@@ -290,12 +333,16 @@ void run_shape(const Shape& s, const Options& o, cublasHandle_t handle, const cu
 
   float z_ms = 0.0f, b_ms = 0.0f;
   if (provider_on(o, "zcutlass")) {
-    z_ms = time_ms(z_fn, o.warmup, o.iterations);
+    z_ms = o.graph ? time_graph_ms(z_fn, o.warmup, o.iterations, stream) : time_ms(z_fn, o.warmup, o.iterations);
     if (out) emit_record(*out, o, s, "zcutlass", zcutlass::selected_kernel_name(desc), z_ms, prop);
   }
   if (provider_on(o, "cublas")) {
-    b_ms = time_ms(blas_fn, o.warmup, o.iterations);
+    b_ms = o.graph ? time_graph_ms(blas_fn, o.warmup, o.iterations, stream) : time_ms(blas_fn, o.warmup, o.iterations);
     if (out) emit_record(*out, o, s, "cublas", "cublasGemmEx", b_ms, prop);
+  }
+  if (stream != nullptr) {
+    CHECK_CUBLAS(cublasSetStream(handle, nullptr));
+    CHECK_CUDA(cudaStreamDestroy(stream));
   }
   const double flops = 2.0 * double(s.m) * s.n * s.k;
   const double z_tf = z_ms > 0 ? flops / (z_ms * 1e-3) / 1e12 : 0.0;
