@@ -70,6 +70,7 @@ FAMILIES = {
     "generic": "_generic",
     "splitk256": "_128x256x64_splitk_cluster",
     "splitk128": "_128x128x64_splitk_cluster",
+    "splitkm256": "_256x256x64_splitk_cluster",
 }
 
 # (m, n, k) per family: ragged edges in every dimension, K tails, multi-tile.
@@ -89,6 +90,7 @@ FAMILY_SHAPES = {
     # cluster split-K: one tile, ragged edges, the cfg0 shape, several tile rows
     "splitk256": [(128, 256, 64), (300, 520, 200), (256, 4096, 4096), (1000, 777, 1032)],
     "splitk128": [(129, 136, 72), (513, 1000, 520), (256, 2048, 1536)],
+    "splitkm256": [(256, 256, 64), (300, 520, 200), (256, 4096, 4096), (1000, 777, 1032), (129, 1024, 2048)],
     # odd leading dimensions (pads 3/5/7/11) on several 128 x 128 tiles, K tails of 1..31
     "generic": [(5, 7, 9), (100, 200, 50), (130, 70, 300), (1000, 777, 1032), (257, 1300, 2101)],
 }
@@ -136,17 +138,17 @@ def test_forced_family(cuda_device, monkeypatch, fam, shape, dt, col):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("splits", [1, 2, 3, 5, 8])
-@pytest.mark.parametrize("bn", [128, 256])
-def test_splitk_split_counts(cuda_device, monkeypatch, splits, bn):
+@pytest.mark.parametrize("tile", ["128x128", "128x256", "256x256"])
+def test_splitk_split_counts(cuda_device, monkeypatch, splits, tile):
     """Every cluster size the split-K kernel can get, on a ragged problem whose
     K blocks do not divide evenly (17 blocks of 64, the last one partial)."""
-    monkeypatch.setenv("ZCUTLASS_FORCE_KERNEL", f"_128x{bn}x64_splitk_cluster")
+    monkeypatch.setenv("ZCUTLASS_FORCE_KERNEL", f"_{tile}x64_splitk_cluster")
     monkeypatch.setenv("ZCUTLASS_SPLITK", str(splits))
     for dt in (F16, BF16):
         for i, (alpha, beta, bias) in enumerate(EPILOGUES):
-            c = Case(f"splitk{bn} s{splits} {i}", dt, 200, 600, 1080, alpha, beta, bias, 0, 0, 0, 8,
+            c = Case(f"splitk{tile} s{splits} {i}", dt, 200, 600, 1080, alpha, beta, bias, 0, 0, 0, 8,
                      b_col_major=(i % 2 == 1), gen="normal", seed=splits * 10 + i)
-            assert FAMILIES[f"splitk{bn}"] in selected(c)["kernel_name"]
+            assert f"_{tile}x64_splitk_cluster" in selected(c)["kernel_name"]
             check_case(c)
 
 

@@ -201,7 +201,9 @@ class Sm100Operation final : public GemmOperation {
       case Kind::UmmaPair:
         return want == PC::Pair256x256;
       case Kind::UmmaSplitK:
-        return want == (desc_.tile_n == 256 ? PC::SplitK128x256 : PC::SplitK128x128);
+        return want == (desc_.tile_m == 256   ? PC::SplitK256x256
+                        : desc_.tile_n == 256 ? PC::SplitK128x256
+                                              : PC::SplitK128x128);
       default:
         return want == (desc_.tile_n == 256 ? PC::Cta128x256 : PC::Cta128x128);
     }
@@ -235,13 +237,15 @@ class Sm100Operation final : public GemmOperation {
         e = zcb::launch_umma_gemm(la, desc_.tile_n);
         break;
       case Kind::UmmaSplitK: {
+        using PC = zcb::PersistentConfig;
         const SelectDevice dev = select_device();
         const zcb::TileChoice tc = zcb::choose_tiles(la.m, la.n, la.k, dev.sm_count);
-        const bool chosen = tc.config == (desc_.tile_n == 256 ? zcb::PersistentConfig::SplitK128x256
-                                                              : zcb::PersistentConfig::SplitK128x128);
-        const int splits = chosen ? tc.splits
-                                  : zcb::splitk_default_splits(la.m, la.n, la.k, desc_.tile_n, dev.sm_count);
-        e = zcb::launch_umma_splitk_gemm(la, desc_.tile_n, splits);
+        const PC mine = desc_.tile_m == 256 ? PC::SplitK256x256 : desc_.tile_n == 256 ? PC::SplitK128x256
+                                                                                      : PC::SplitK128x128;
+        const int splits = tc.config == mine ? tc.splits
+                                             : zcb::splitk_default_splits(la.m, la.n, la.k, desc_.tile_m,
+                                                                          desc_.tile_n, dev.sm_count);
+        e = zcb::launch_umma_splitk_gemm(la, desc_.tile_m, desc_.tile_n, splits);
         break;
       }
       case Kind::UmmaSwapAbStreamK:
@@ -270,7 +274,7 @@ void register_builtin_operations() {
   using F = ShapeFamily;
   using E = EpilogueKind;
   // First match wins: small-M swap-AB buckets, then the cluster split-K and
-  // persistent kernels (split-K 128x256 / 128x128, CTA-pair 256x256, or
+  // persistent kernels (split-K 256x256 / 128x256 / 128x128, CTA-pair 256x256, or
   // one-CTA 128x256 / 128x128 tiles, whichever the cost model in
   // choose_tiles picks), then the predicated CUDA-core kernel that accepts
   // any layout.
@@ -287,6 +291,8 @@ void register_builtin_operations() {
       {"zcutlass_sm100_tcgen05_f16_32x128x64_swapab_splitk", DType::F16, K::UmmaSwapAb, 32, 128, 64, 9, F::Decode, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_bf16_64x128x64_swapab_splitk", DType::BF16, K::UmmaSwapAb, 64, 128, 64, 7, F::Prefill, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_f16_64x128x64_swapab_splitk", DType::F16, K::UmmaSwapAb, 64, 128, 64, 7, F::Prefill, E::RegisterLinear},
+      {"zcutlass_sm100_tcgen05_bf16_256x256x64_splitk_cluster", DType::BF16, K::UmmaSplitK, 256, 256, 64, 3, F::Prefill, E::RegisterLinear},
+      {"zcutlass_sm100_tcgen05_f16_256x256x64_splitk_cluster", DType::F16, K::UmmaSplitK, 256, 256, 64, 3, F::Prefill, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_bf16_128x256x64_splitk_cluster", DType::BF16, K::UmmaSplitK, 128, 256, 64, 4, F::Prefill, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_f16_128x256x64_splitk_cluster", DType::F16, K::UmmaSplitK, 128, 256, 64, 4, F::Prefill, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_bf16_128x128x64_splitk_cluster", DType::BF16, K::UmmaSplitK, 128, 128, 64, 6, F::Prefill, E::RegisterLinear},

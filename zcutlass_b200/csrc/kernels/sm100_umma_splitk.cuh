@@ -4,20 +4,23 @@
 //
 //   D[M,N] = alpha * A[M,K] * B[K,N] + beta * C[M,N] + bias[N]     (row-major, f16/bf16)
 //
-// One thread-block cluster of S CTAs computes one 128 x BN output tile; CTA r
+// One thread-block cluster of S CTAs computes one BM x BN output tile; CTA r
 // of the cluster runs K blocks [r*KB/S, (r+1)*KB/S) through the same
 // warp-specialised pipeline as the persistent kernel (warp 0 TMA producer,
-// warp 1 MMA issuer with a BN-column TMEM accumulator, warps 2-5 epilogue).
-// Afterwards:
-//   1. the epilogue warps copy the FP32 partial tile from TMEM into this CTA's
-//      shared memory ([128][BN + 4] floats, over the drained pipeline ring);
-//   2. cluster barrier: every partial is in place;
-//   3. CTA r owns rows [r*128/S, (r+1)*128/S) of the tile: each thread reads a
+// warp 1 MMA issuer, warps 2-5 epilogue). With BM = 256 the CTA holds two
+// 128 x BN accumulators in TMEM (all 512 columns for BN = 256) and every B
+// tile it loads feeds both, which halves the bytes the SM's TMA unit moves
+// per FLOP -- the limit for these HBM-streaming shapes. Afterwards, for each
+// 128-row half h of the tile:
+//   1. the epilogue warps copy half h of the FP32 partial from TMEM into this
+//      CTA's shared memory ([128][BN + 4] floats, over the drained ring);
+//   2. cluster barrier: every CTA's half h is in place;
+//   3. CTA r owns rows [r*128/S, (r+1)*128/S) of the half: each thread reads a
 //      4-column group of its rows from every CTA's partial through distributed
 //      shared memory (ld.shared::cluster.v4), adds them in CTA order -- the
 //      sum does not depend on timing -- applies alpha/beta/bias, rounds once
 //      and stores 4 outputs (8 bytes) to D;
-//   4. cluster barrier: no CTA leaves while a peer still reads its partial.
+//   4. cluster barrier: no CTA overwrites or leaves while a peer still reads.
 // No global scratch memory is used. Ragged M/N/K: TMA zero-fills loads
 // outside A and B; rows and columns outside D are never stored.
 #pragma once
@@ -49,10 +52,11 @@ constexpr int kUmmaK = 16;
 constexpr int kThreads = 192;
 constexpr int kEpiWarps = 4;
 constexpr int kMaxSplits = 8;  // portable cluster size
+constexpr int kUnroll = 2;     // reduction groups per thread per pass
 
-template <int BN, int STAGES>
+template <int BM, int BN, int STAGES>
 struct Smem {
-  static constexpr int kABytes = kBlockM * kBlockK * 2;     // 16 KiB
+  static constexpr int kABytes = BM * kBlockK * 2;          // 16 or 32 KiB
   static constexpr int kBChunkBytes = kBlockK * 128;        // 64(n) x 64(k) box: 8 KiB
   static constexpr int kBBytes = (BN / 64) * kBChunkBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -69,6 +73,7 @@ struct Smem {
   static constexpr int kBytes = kMiscOff + 16;
   static constexpr int kDynamicBytes = kBytes + 1024;
   static_assert(BN == 128 || BN == 256, "BN must be 128 or 256");
+  static_assert(BM == 128 || BM == 256, "BM must be 128 or 256");
   static_assert(kRedBytes <= kRingBytes, "the partial tile must fit in the drained pipeline ring");
   static_assert(kDynamicBytes <= 232448, "shared memory budget exceeded");
 };
@@ -95,13 +100,53 @@ __device__ __forceinline__ float4 load4(const T* p) {
   return make_float4(lo.x, lo.y, hi.x, hi.y);
 }
 
+// Epilogue of 4 consecutive outputs of one row: alpha * sum (+ beta * C)
+// (+ bias), rounded once; an 8-byte store when all 4 are inside N.
+template <typename T>
+__device__ __forceinline__ void store_group(T* dptr, const T* cptr, const T* bptr, const SplitKParams& p, bool has_c,
+                                            bool has_bias, int row, int col, const float4& sum) {
+  float v[4] = {p.alpha * sum.x, p.alpha * sum.y, p.alpha * sum.z, p.alpha * sum.w};
+  const int valid = p.n - col < 4 ? p.n - col : 4;
+  if (valid == 4) {
+    if (has_c) {
+      const float4 cv = load4(cptr + static_cast<int64_t>(row) * p.ldc + col);
+      v[0] += p.beta * cv.x;
+      v[1] += p.beta * cv.y;
+      v[2] += p.beta * cv.z;
+      v[3] += p.beta * cv.w;
+    }
+    if (has_bias) {
+      const float4 bv = load4(bptr + col);
+      v[0] += bv.x;
+      v[1] += bv.y;
+      v[2] += bv.z;
+      v[3] += bv.w;
+    }
+    uint2 out;
+    out.x = Elem<T>::pack(v[0], v[1]);
+    out.y = Elem<T>::pack(v[2], v[3]);
+    *reinterpret_cast<uint2*>(dptr + static_cast<int64_t>(row) * p.ldd + col) = out;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (j < valid) {
+        float x = v[j];
+        if (has_c) x += p.beta * Elem<T>::to_float(cptr[static_cast<int64_t>(row) * p.ldc + col + j]);
+        if (has_bias) x += Elem<T>::to_float(bptr[col + j]);
+        dptr[static_cast<int64_t>(row) * p.ldd + col + j] = Elem<T>::from_float(x);
+      }
+    }
+  }
+}
+
 // kBKMajor: B is column-major (a PyTorch [N, K] weight): its tiles are K-major.
-template <typename T, int BN, int STAGES, bool kBKMajor>
+template <typename T, int BM, int BN, int STAGES, bool kBKMajor>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                 const SplitKParams p) {
-  using L = Smem<BN, STAGES>;
-  constexpr uint32_t kTmemCols = BN;
+  using L = Smem<BM, BN, STAGES>;
+  constexpr int kHalves = BM / kBlockM;
+  constexpr uint32_t kTmemCols = kHalves * BN;  // accumulator h at columns [h*BN, (h+1)*BN)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -117,7 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();  // the cluster spans gridDim.x == p.splits
   const int n0 = blockIdx.y * BN;
-  const int m0 = blockIdx.z * kBlockM;
+  const int m0 = blockIdx.z * BM;
   const int kb_begin = static_cast<int>((static_cast<int64_t>(rank) * p.num_kb) / p.splits);
   const int kb_end = static_cast<int>((static_cast<int64_t>(rank + 1) * p.num_kb) / p.splits);
 
@@ -146,6 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   griddep_wait();  // inputs/outputs may belong to the previous kernel on the stream
   griddep_launch_dependents();
   const WaitCtx ctx{abort_flag, p.error_word};
+  bool epi_ok = false;  // epilogue warps: the accumulator is complete
 
   if (warp == 0) {
     if (lane == 0) {
@@ -190,10 +236,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t b_addr = smem_addr(smem + L::kBOff + s * L::kBBytes);
 #pragma unroll
         for (int kk = 0; kk < kBlockK / kUmmaK; ++kk) {
-          const uint64_t a_desc = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
           const uint64_t b_desc = kBKMajor ? smem_desc_sw128(b_addr + kk * 32, 16, 1024)
                                            : smem_desc_sw128(b_addr + kk * 2048, L::kBChunkBytes, 1024);
-          umma_f16_ss(tmem_base, a_desc, b_desc, kIdesc, (it | kk) != 0 ? 1u : 0u);
+#pragma unroll
+          for (int h = 0; h < kHalves; ++h) {  // rows [128h, 128h + 128) of the A tile: 16 KiB apart
+            const uint64_t a_desc = smem_desc_sw128(a_addr + h * 16384 + kk * 32, 16, 1024);
+            umma_f16_ss(tmem_base + h * BN, a_desc, b_desc, kIdesc, (it | kk) != 0 ? 1u : 0u);
+          }
         }
         issued = true;
         umma_commit(&empty[s]);
@@ -209,107 +258,99 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // Partial tile from TMEM to shared memory: thread = row of the tile.
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const bool ok = mbar_wait(tmem_full, 0, ctx, kErrEpiTmemFull);
-    if (__all_sync(0xffffffffu, ok)) {
+    epi_ok = mbar_wait(tmem_full, 0, ctx, kErrEpiTmemFull);
+    epi_ok = __all_sync(0xffffffffu, epi_ok);
+  }
+
+  const T* cptr = static_cast<const T*>(p.c);
+  const T* bptr = static_cast<const T*>(p.bias);
+  T* dptr = static_cast<T*>(p.d);
+  const bool has_c = (p.epi_flags & kEpiHasC) != 0;
+  const bool has_bias = (p.epi_flags & kEpiHasBias) != 0;
+  const int r_begin = static_cast<int>((rank * kBlockM) / p.splits);
+  const int r_end = static_cast<int>(((rank + 1) * kBlockM) / p.splits);
+  constexpr int kGroups = BN / 4;  // 4-column groups per row
+  const int total = (r_end - r_begin) * kGroups;
+  const uint32_t red_addr = smem_addr(red);
+
+#pragma unroll 1
+  for (int h = 0; h < kHalves; ++h) {
+    // Half h of the partial from TMEM to shared memory: thread = row of the half.
+    if (warp >= 2 && epi_ok) {
       tc_fence_after_sync();
+      const int quarter = warp & 3;
+      const int row = quarter * 32 + lane;
       float4* dst = reinterpret_cast<float4*>(red + row * L::kRedStride);
       if (kb_end > kb_begin) {
-        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + h * BN;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t acc[32];
-          tmem_ld_32x32b_x32(taddr + c * 32, acc);
+        for (int c = 0; c < BN / 32; c += 2) {  // two 32-column loads in flight per wait
+          uint32_t acc[2][32];
+          tmem_ld_32x32b_x32(taddr + c * 32, acc[0]);
+          tmem_ld_32x32b_x32(taddr + (c + 1) * 32, acc[1]);
           tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            dst[c * 8 + j] = make_float4(__uint_as_float(acc[4 * j]), __uint_as_float(acc[4 * j + 1]),
-                                         __uint_as_float(acc[4 * j + 2]), __uint_as_float(acc[4 * j + 3]));
+          for (int q = 0; q < 2; ++q)
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              dst[(c + q) * 8 + j] = make_float4(__uint_as_float(acc[q][4 * j]), __uint_as_float(acc[q][4 * j + 1]),
+                                                 __uint_as_float(acc[q][4 * j + 2]), __uint_as_float(acc[q][4 * j + 3]));
         }
       } else {
 #pragma unroll 4
         for (int j = 0; j < BN / 4; ++j) dst[j] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
-  }
 
-  // Every thread of every CTA reaches both cluster barriers, on the abort
-  // path too, so no CTA waits for a peer that left.
-  tc_fence_before_sync();
-  __syncwarp();
-  cluster_sync_all();
+    // Every thread of every CTA reaches both cluster barriers of every half,
+    // on the abort path too, so no CTA waits for a peer that left.
+    tc_fence_before_sync();
+    __syncwarp();
+    cluster_sync_all();
 
-  if (*abort_flag == 0) {  // an aborted CTA has no partial; its error code is already recorded
-    const T* cptr = static_cast<const T*>(p.c);
-    const T* bptr = static_cast<const T*>(p.bias);
-    T* dptr = static_cast<T*>(p.d);
-    const bool has_c = (p.epi_flags & kEpiHasC) != 0;
-    const bool has_bias = (p.epi_flags & kEpiHasBias) != 0;
-    const int r_begin = static_cast<int>((rank * kBlockM) / p.splits);
-    const int r_end = static_cast<int>(((rank + 1) * kBlockM) / p.splits);
-    constexpr int kGroups = BN / 4;  // 4-column groups per row
-    const int total = (r_end - r_begin) * kGroups;
-    const uint32_t red_addr = smem_addr(red);
+    if (*abort_flag == 0) {  // an aborted CTA has no partial; its error code is already recorded
+      // kUnroll groups per thread per pass, every DSMEM load of the pass issued
+      // before the first sum: the remote-load latency is paid once per pass.
 #pragma unroll 1
-    for (int g = threadIdx.x; g < total; g += kThreads) {
-      const int rl = r_begin + g / kGroups;
-      const int cl = (g % kGroups) * 4;
-      const int row = m0 + rl, col = n0 + cl;
-      if (row >= p.m || col >= p.n) continue;
-      const uint32_t off = static_cast<uint32_t>((rl * L::kRedStride + cl) * 4);
-      float4 part[kMaxSplits];  // every remote load first: one DSMEM round trip
+      for (int g0 = threadIdx.x; g0 < total; g0 += kThreads * kUnroll) {
+        float4 part[kUnroll][kMaxSplits];
 #pragma unroll
-      for (int s = 0; s < kMaxSplits; ++s)
-        if (s < p.splits) part[s] = ld_dsmem_v4(red_addr + off, static_cast<uint32_t>(s));
-      float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int u = 0; u < kUnroll; ++u) {
+          const int g = g0 + u * kThreads;
+          if (g >= total) continue;
+          const int rl = r_begin + g / kGroups;
+          const int cl = (g % kGroups) * 4;
+          const uint32_t off = static_cast<uint32_t>((rl * L::kRedStride + cl) * 4);
 #pragma unroll
-      for (int s = 0; s < kMaxSplits; ++s) {
-        if (s < p.splits) {
-          sum.x += part[s].x;
-          sum.y += part[s].y;
-          sum.z += part[s].z;
-          sum.w += part[s].w;
+          for (int s = 0; s < kMaxSplits; ++s)
+            if (s < p.splits) part[u][s] = ld_dsmem_v4(red_addr + off, static_cast<uint32_t>(s));
         }
-      }
-      float v[4] = {p.alpha * sum.x, p.alpha * sum.y, p.alpha * sum.z, p.alpha * sum.w};
-      const int valid = p.n - col < 4 ? p.n - col : 4;
-      if (valid == 4) {
-        if (has_c) {
-          const float4 cv = load4(cptr + static_cast<int64_t>(row) * p.ldc + col);
-          v[0] += p.beta * cv.x;
-          v[1] += p.beta * cv.y;
-          v[2] += p.beta * cv.z;
-          v[3] += p.beta * cv.w;
-        }
-        if (has_bias) {
-          const float4 bv = load4(bptr + col);
-          v[0] += bv.x;
-          v[1] += bv.y;
-          v[2] += bv.z;
-          v[3] += bv.w;
-        }
-        uint2 out;
-        out.x = Elem<T>::pack(v[0], v[1]);
-        out.y = Elem<T>::pack(v[2], v[3]);
-        *reinterpret_cast<uint2*>(dptr + static_cast<int64_t>(row) * p.ldd + col) = out;
-      } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if (j < valid) {
-            float x = v[j];
-            if (has_c) x += p.beta * Elem<T>::to_float(cptr[static_cast<int64_t>(row) * p.ldc + col + j]);
-            if (has_bias) x += Elem<T>::to_float(bptr[col + j]);
-            dptr[static_cast<int64_t>(row) * p.ldd + col + j] = Elem<T>::from_float(x);
+        for (int u = 0; u < kUnroll; ++u) {
+          const int g = g0 + u * kThreads;
+          if (g >= total) continue;
+          const int rl = r_begin + g / kGroups;
+          const int cl = (g % kGroups) * 4;
+          const int row = m0 + h * kBlockM + rl, col = n0 + cl;
+          if (row >= p.m || col >= p.n) continue;
+          float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int s = 0; s < kMaxSplits; ++s) {
+            if (s < p.splits) {  // in CTA order: the result does not depend on timing
+              sum.x += part[u][s].x;
+              sum.y += part[u][s].y;
+              sum.z += part[u][s].z;
+              sum.w += part[u][s].w;
+            }
           }
+          store_group<T>(dptr, cptr, bptr, p, has_c, has_bias, row, col, sum);
         }
       }
     }
+    __syncwarp();
+    cluster_sync_all();  // peers are done reading this half before it is overwritten or freed
   }
 
-  __syncwarp();
-  cluster_sync_all();
   if (warp == 1) {
     tc_fence_after_sync();
     tmem_dealloc(tmem_base, kTmemCols);

@@ -39,6 +39,7 @@ constexpr int kBlockN = 128;  // rows of D^T per CTA (MMA M)
 constexpr int kBlockK = 64;   // one 128-byte swizzle row of K; a stage holds KSUB of them
 constexpr int kThreads = 192;
 constexpr int kMaxSplits = 8;  // cluster size limit (portable)
+constexpr int kRedUnroll = 4;  // reduction elements per thread per pass
 
 // A pipeline stage holds KSUB K sub-blocks of 64: TMA streams a weight
 // matrix at ~4.7 TB/s with 16 KiB per stage but ~5.7 TB/s with >= 32 KiB
@@ -245,25 +246,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int rows = r_end - r_begin;
     const int tid = threadIdx.x - 64;
     const uint32_t red_addr = smem_addr(red);
-    for (int idx = tid; idx < rows * p.m; idx += 128) {
-      const int mi = idx / rows;
-      const int rl = r_begin + idx % rows;
-      const int n = n0 + rl;
-      if (n >= p.n) continue;
-      const uint32_t off = static_cast<uint32_t>((mi * kBlockN + rl) * 4);
-      // all of an element's remote loads first (one DSMEM round trip, not S)
-      float part[kMaxSplits];
+    const int total = rows * p.m;
+    // kRedUnroll elements per thread per pass, every remote load of the pass
+    // issued before the first sum: the DSMEM latency is paid once per pass.
+#pragma unroll 1
+    for (int i0 = tid; i0 < total; i0 += 128 * kRedUnroll) {
+      float part[kRedUnroll][kMaxSplits];
 #pragma unroll
-      for (int s = 0; s < kMaxSplits; ++s)
-        part[s] = s < p.splits ? ld_dsmem_f32(red_addr + off, static_cast<uint32_t>(s)) : 0.0f;
-      float sum = 0.0f;  // in split order, as before: the result does not depend on timing
+      for (int u = 0; u < kRedUnroll; ++u) {
+        const int idx = i0 + u * 128;
+        if (idx >= total) continue;
+        const uint32_t off = static_cast<uint32_t>(((idx / rows) * kBlockN + r_begin + idx % rows) * 4);
 #pragma unroll
-      for (int s = 0; s < kMaxSplits; ++s)
-        if (s < p.splits) sum += part[s];
-      float v = p.alpha * sum;
-      if (has_c) v += p.beta * Elem<T>::to_float(cptr[static_cast<int64_t>(mi) * p.ldc + n]);
-      if (has_bias) v += Elem<T>::to_float(bptr[n]);
-      dptr[static_cast<int64_t>(mi) * p.ldd + n] = Elem<T>::from_float(v);
+        for (int s = 0; s < kMaxSplits; ++s)
+          part[u][s] = s < p.splits ? ld_dsmem_f32(red_addr + off, static_cast<uint32_t>(s)) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < kRedUnroll; ++u) {
+        const int idx = i0 + u * 128;
+        if (idx >= total) continue;
+        const int mi = idx / rows;
+        const int n = n0 + r_begin + idx % rows;
+        if (n >= p.n) continue;
+        float sum = 0.0f;  // in split order: the result does not depend on timing
+#pragma unroll
+        for (int s = 0; s < kMaxSplits; ++s)
+          if (s < p.splits) sum += part[u][s];
+        float v = p.alpha * sum;
+        if (has_c) v += p.beta * Elem<T>::to_float(cptr[static_cast<int64_t>(mi) * p.ldc + n]);
+        if (has_bias) v += Elem<T>::to_float(bptr[n]);
+        dptr[static_cast<int64_t>(mi) * p.ldd + n] = Elem<T>::from_float(v);
+      }
     }
   }
 

@@ -285,16 +285,16 @@ cudaError_t launch_umma2_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit
   return cudaGetLastError();
 }
 
-template <typename T, int BN, int STAGES, bool KM>
+template <typename T, int BM, int BN, int STAGES, bool KM>
 cudaError_t launch_splitk_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit, int splits) {
-  using L = splitk::Smem<BN, STAGES>;
+  using L = splitk::Smem<BM, BN, STAGES>;
   CUtensorMap ta, tb;
   const bool bf16 = a.bf16;
   const bool b_ok = KM ? make_tma_2d(&tb, a.b, bf16, a.n, a.k, a.ldb, BN, splitk::kBlockK, TmaSwizzle::B128)
                        : make_tma_2d(&tb, a.b, bf16, a.k, a.n, a.ldb, splitk::kBlockK, 64, TmaSwizzle::B128);
-  if (!b_ok || !make_tma_2d(&ta, a.a, bf16, a.m, a.k, a.lda, splitk::kBlockM, splitk::kBlockK, TmaSwizzle::B128))
+  if (!b_ok || !make_tma_2d(&ta, a.a, bf16, a.m, a.k, a.lda, BM, splitk::kBlockK, TmaSwizzle::B128))
     return cudaErrorInvalidValue;
-  const int64_t tiles_m = (a.m + splitk::kBlockM - 1) / splitk::kBlockM;
+  const int64_t tiles_m = (a.m + BM - 1) / BM;
   const int64_t tiles_n = (a.n + BN - 1) / BN;
   if (tiles_m > 65535 || tiles_n > 65535) return cudaErrorInvalidValue;
   SplitKParams p{};
@@ -312,7 +312,7 @@ cudaError_t launch_splitk_t(const LaunchArgs& a, DeviceSlot* slot, int config_bi
   p.epi_flags = (a.beta != 0.0f ? kEpiHasC : 0u) | (a.bias != nullptr ? kEpiHasBias : 0u);
   p.error_word = slot->info.error_word;
 
-  auto kernel = splitk::gemm_kernel<T, BN, STAGES, KM>;
+  auto kernel = splitk::gemm_kernel<T, BM, BN, STAGES, KM>;
   cudaError_t e = ensure_smem_attr(slot, config_bit, kernel, L::kDynamicBytes);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg{};
@@ -516,6 +516,8 @@ enum : int {
   kCfgSplitKF16N256,
   kCfgSplitKBf16N128,
   kCfgSplitKF16N128,
+  kCfgSplitKBf16M256,
+  kCfgSplitKF16M256,
   kCfgColMajorB = 32,
 };
 
@@ -546,14 +548,18 @@ cudaError_t launch_umma_km(const LaunchArgs& a, DeviceSlot* slot, int bn) {
 }
 
 template <bool KM>
-cudaError_t launch_splitk_km(const LaunchArgs& a, DeviceSlot* slot, int bn, int splits) {
+cudaError_t launch_splitk_km(const LaunchArgs& a, DeviceSlot* slot, int bm, int bn, int splits) {
   const int off = KM ? kCfgColMajorB : 0;
-  if (bn == 256) {
-    return a.bf16 ? launch_splitk_t<__nv_bfloat16, 256, 4, KM>(a, slot, kCfgSplitKBf16N256 + off, splits)
-                  : launch_splitk_t<half, 256, 4, KM>(a, slot, kCfgSplitKF16N256 + off, splits);
+  if (bm == 256) {
+    return a.bf16 ? launch_splitk_t<__nv_bfloat16, 256, 256, 3, KM>(a, slot, kCfgSplitKBf16M256 + off, splits)
+                  : launch_splitk_t<half, 256, 256, 3, KM>(a, slot, kCfgSplitKF16M256 + off, splits);
   }
-  return a.bf16 ? launch_splitk_t<__nv_bfloat16, 128, 6, KM>(a, slot, kCfgSplitKBf16N128 + off, splits)
-                : launch_splitk_t<half, 128, 6, KM>(a, slot, kCfgSplitKF16N128 + off, splits);
+  if (bn == 256) {
+    return a.bf16 ? launch_splitk_t<__nv_bfloat16, 128, 256, 4, KM>(a, slot, kCfgSplitKBf16N256 + off, splits)
+                  : launch_splitk_t<half, 128, 256, 4, KM>(a, slot, kCfgSplitKF16N256 + off, splits);
+  }
+  return a.bf16 ? launch_splitk_t<__nv_bfloat16, 128, 128, 6, KM>(a, slot, kCfgSplitKBf16N128 + off, splits)
+                : launch_splitk_t<half, 128, 128, 6, KM>(a, slot, kCfgSplitKF16N128 + off, splits);
 }
 
 template <bool KM>
@@ -578,46 +584,69 @@ const DeviceInfo* current_device_info() {
   return slot ? &slot->info : nullptr;
 }
 
+// Per-SM time of one K block (64 deep) of a tile, in SM clocks: the larger of
+// the tensor-core time (about 5650 dense FLOP per clock per SM, the measured
+// burst cuBLAS rate) and the TMA time (about 43 B per clock per SM, the
+// streaming rate measured for these kernels). `rows` x `cols` is the part of
+// the tile one SM computes; `load_bytes` what its TMA unit loads per block.
+double kblock_clocks(double rows, double cols, double load_bytes) {
+  const double mma = rows * cols * 64.0 * 2.0 / 5650.0;
+  const double tma = load_bytes / 43.0;
+  return mma > tma ? mma : tma;
+}
+
 TileChoice choose_tiles(int64_t m, int64_t n, int64_t k, int sm_count) {
-  // Persistent configurations: waves x tile area / efficiency, as in
-  // choose_persistent, times the full K. Split-K configurations (one wave of
-  // tiles x S clusters' CTAs): tile area x (K/S + the reduction, costed as two
-  // K blocks) / the same efficiency. Split-K only competes when the tiles
-  // alone fill at most half the SMs.
+  // Persistent tiles: waves x K blocks x per-block time. Split-K tiles (one
+  // wave of tiles x S CTAs): (K blocks / S + 2, the DSMEM reduction) x
+  // per-block time. The model reproduces the measured 8192 x 28672 x 4096
+  // (1.22 ms modelled, 1.27 ms measured) and 256 x 4096 x 4096 on 128 x 128
+  // persistent tiles (24.8 us modelled, 23.9 measured).
   const int64_t kb = (k + 63) / 64;
-  const PersistentConfig base = choose_persistent(m, n, sm_count);
-  const auto persistent_cost = [&](PersistentConfig c) {
-    const int tm = c == PersistentConfig::Pair256x256 ? 256 : 128;
-    const int tn = c == PersistentConfig::Cta128x128 ? 128 : 256;
-    const int units = c == PersistentConfig::Pair256x256 ? sm_count / 2 : sm_count;
-    const double area = c == PersistentConfig::Pair256x256 ? 256.0 * 256.0 / 2.0 : double(tm) * tn;
-    const double eff = c == PersistentConfig::Pair256x256 ? 1.0 : c == PersistentConfig::Cta128x256 ? 0.86 : 0.72;
-    const int64_t tiles = ((m + tm - 1) / tm) * ((n + tn - 1) / tn);
-    return double((tiles + units - 1) / units) * area * double(kb) / eff;
+  struct Cand {
+    PersistentConfig cfg;
+    int tile_m, tile_n, units;  // units: CTAs (or CTA pairs) resident at once
+    double per_kb;
+    bool split;
   };
-  TileChoice best{base, 1};
-  double best_cost = persistent_cost(base);
+  const int pairs = sm_count / 2;
+  const Cand cands[] = {
+      {PersistentConfig::Pair256x256, 256, 256, pairs, kblock_clocks(128, 256, 256 * 128), false},
+      {PersistentConfig::Cta128x256, 128, 256, sm_count, kblock_clocks(128, 256, 384 * 128), false},
+      {PersistentConfig::Cta128x128, 128, 128, sm_count, kblock_clocks(128, 128, 256 * 128), false},
+      {PersistentConfig::SplitK256x256, 256, 256, sm_count, kblock_clocks(256, 256, 512 * 128), true},
+      {PersistentConfig::SplitK128x256, 128, 256, sm_count, kblock_clocks(128, 256, 384 * 128), true},
+      {PersistentConfig::SplitK128x128, 128, 128, sm_count, kblock_clocks(128, 128, 256 * 128), true},
+  };
   const char* forced = std::getenv("ZCUTLASS_SPLITK");
   const int forced_splits = forced != nullptr ? std::atoi(forced) : 0;
-  for (const int bn : {256, 128}) {
-    const int64_t tiles = ((m + 127) / 128) * ((n + bn - 1) / bn);
-    if (tiles <= 0 || tiles * 2 > sm_count || kb <= 0) continue;
-    int64_t s = std::min<int64_t>({int64_t(splitk::kMaxSplits), sm_count / tiles, kb / 2});
-    if (forced_splits > 0) s = std::min<int64_t>(std::min<int64_t>(forced_splits, splitk::kMaxSplits), kb);
-    if (s < 2) continue;
-    const double eff = bn == 256 ? 0.86 : 0.72;
-    const double cost = 128.0 * bn * (double((kb + s - 1) / s) + 2.0) / eff;
+  TileChoice best{choose_persistent(m, n, sm_count), 1};
+  double best_cost = 1e300;
+  for (const Cand& c : cands) {
+    const int64_t tiles = ((m + c.tile_m - 1) / c.tile_m) * ((n + c.tile_n - 1) / c.tile_n);
+    if (tiles <= 0 || kb <= 0) continue;
+    double cost;
+    int splits = 1;
+    if (!c.split) {
+      cost = double((tiles + c.units - 1) / c.units) * double(kb) * c.per_kb;
+    } else {
+      if (tiles * 2 > sm_count) continue;  // split-K only when the tiles alone leave SMs idle
+      int64_t s = std::min<int64_t>({int64_t(splitk::kMaxSplits), sm_count / tiles, kb / 2});
+      if (forced_splits > 0) s = std::min<int64_t>(std::min<int64_t>(forced_splits, splitk::kMaxSplits), kb);
+      if (s < 2) continue;
+      splits = static_cast<int>(s);
+      cost = (double((kb + s - 1) / s) + 2.0) * c.per_kb;
+    }
     if (cost < best_cost * 0.999) {
       best_cost = cost;
-      best = {bn == 256 ? PersistentConfig::SplitK128x256 : PersistentConfig::SplitK128x128, static_cast<int>(s)};
+      best = {c.cfg, splits};
     }
   }
   return best;
 }
 
-int splitk_default_splits(int64_t m, int64_t n, int64_t k, int bn, int sm_count) {
+int splitk_default_splits(int64_t m, int64_t n, int64_t k, int bm, int bn, int sm_count) {
   const int64_t kb = (k + 63) / 64;
-  const int64_t tiles = std::max<int64_t>(1, ((m + 127) / 128) * ((n + bn - 1) / bn));
+  const int64_t tiles = std::max<int64_t>(1, ((m + bm - 1) / bm) * ((n + bn - 1) / bn));
   const char* forced = std::getenv("ZCUTLASS_SPLITK");
   int64_t s = forced != nullptr && std::atoi(forced) > 0 ? std::atoi(forced) : sm_count / tiles;
   s = std::min<int64_t>({s, int64_t(splitk::kMaxSplits), kb});
@@ -678,10 +707,11 @@ cudaError_t launch_umma_gemm(const LaunchArgs& a, int bn) {
   return a.b_col_major ? launch_umma_km<true>(a, slot, bn) : launch_umma_km<false>(a, slot, bn);
 }
 
-cudaError_t launch_umma_splitk_gemm(const LaunchArgs& a, int bn, int splits) {
+cudaError_t launch_umma_splitk_gemm(const LaunchArgs& a, int bm, int bn, int splits) {
   DeviceSlot* slot = current_slot();
   if (slot == nullptr) return cudaErrorInvalidDevice;
-  return a.b_col_major ? launch_splitk_km<true>(a, slot, bn, splits) : launch_splitk_km<false>(a, slot, bn, splits);
+  return a.b_col_major ? launch_splitk_km<true>(a, slot, bm, bn, splits)
+                       : launch_splitk_km<false>(a, slot, bm, bn, splits);
 }
 
 cudaError_t launch_umma_pair_gemm(const LaunchArgs& a) {

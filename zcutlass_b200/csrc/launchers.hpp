@@ -62,12 +62,13 @@ bool swapab_sk_ready_for_stream(int64_t m, int64_t n, int64_t k, cudaStream_t st
 // Predicated CUDA-core kernel for TMA-incompatible layouts.
 cudaError_t launch_generic_gemm(const LaunchArgs& args);
 
-// Cluster split-K tcgen05 kernel, one 128 x bn tile (bn in {128, 256}) per
-// cluster of `splits` CTAs along K, reduced through distributed shared memory.
-cudaError_t launch_umma_splitk_gemm(const LaunchArgs& args, int bn, int splits);
+// Cluster split-K tcgen05 kernel, one bm x bn tile (128 x 128, 128 x 256 or
+// 256 x 256) per cluster of `splits` CTAs along K, reduced through distributed
+// shared memory.
+cudaError_t launch_umma_splitk_gemm(const LaunchArgs& args, int bm, int bn, int splits);
 
 // Shape heuristics shared by dispatch and telemetry.
-enum class PersistentConfig { Pair256x256, Cta128x256, Cta128x128, SplitK128x256, SplitK128x128 };
+enum class PersistentConfig { Pair256x256, Cta128x256, Cta128x128, SplitK256x256, SplitK128x256, SplitK128x128 };
 // The persistent configurations only (no split-K): for paths whose kernels
 // need one CTA (pair) per output tile.
 PersistentConfig choose_persistent(int64_t m, int64_t n, int sm_count);
@@ -78,10 +79,10 @@ struct TileChoice {
 // Every configuration, split-K included; ZCUTLASS_SPLITK=<s> fixes the split
 // count of the split-K configurations (tests).
 TileChoice choose_tiles(int64_t m, int64_t n, int64_t k, int sm_count);
-// Split count for a split-K launch of 128 x bn tiles when the kernel is used
+// Split count for a split-K launch of bm x bn tiles when the kernel is used
 // outside choose_tiles' choice (forced): ZCUTLASS_SPLITK, else as many CTAs
 // per tile as the SMs allow, at most 8 and at most one per K block.
-int splitk_default_splits(int64_t m, int64_t n, int64_t k, int bn, int sm_count);
+int splitk_default_splits(int64_t m, int64_t n, int64_t k, int bm, int bn, int sm_count);
 int swapab_choose_splits(int64_t n, int64_t k, int sm_count);
 
 // In-place NVLS all-reduce (sum) of `nbytes` of f16/bf16 at multicast
