@@ -584,23 +584,16 @@ const DeviceInfo* current_device_info() {
   return slot ? &slot->info : nullptr;
 }
 
-// Per-SM time of one K block (64 deep) of a tile, in SM clocks: the larger of
-// the tensor-core time (about 5650 dense FLOP per clock per SM, the measured
-// burst cuBLAS rate) and the TMA time (about 43 B per clock per SM, the
-// streaming rate measured for these kernels). `rows` x `cols` is the part of
-// the tile one SM computes; `load_bytes` what its TMA unit loads per block.
-double kblock_clocks(double rows, double cols, double load_bytes) {
-  const double mma = rows * cols * 64.0 * 2.0 / 5650.0;
-  const double tma = load_bytes / 43.0;
-  return mma > tma ? mma : tma;
-}
-
 TileChoice choose_tiles(int64_t m, int64_t n, int64_t k, int sm_count) {
-  // Persistent tiles: waves x K blocks x per-block time. Split-K tiles (one
-  // wave of tiles x S CTAs): (K blocks / S + 2, the DSMEM reduction) x
-  // per-block time. The model reproduces the measured 8192 x 28672 x 4096
-  // (1.22 ms modelled, 1.27 ms measured) and 256 x 4096 x 4096 on 128 x 128
-  // persistent tiles (24.8 us modelled, 23.9 measured).
+  // Time model in SM clocks, calibrated on B200 from per-CTA phase timestamps
+  // and graph-timed runs (bf16, 148 SMs):
+  //   persistent: waves x K blocks x clocks per K block of one tile
+  //     (CTA pair 256x256: 800, 128x256: 870, 128x128: 690);
+  //   split-K (one wave): ceil(K blocks / S) x clocks per K block (128-row
+  //     tiles 570, 256x256: 1000) + the cross-CTA reduction, which moves the
+  //     whole FP32 partial through distributed shared memory: 3000 + BM*BN/4.
+  // The model reproduces the measured order of the configurations on 256 x
+  // {1024..8192}^2, 512 / 1024 x 4096^2, 2048 x 1536^2 and 8192 x 28672 x 4096.
   const int64_t kb = (k + 63) / 64;
   struct Cand {
     PersistentConfig cfg;
@@ -610,12 +603,12 @@ TileChoice choose_tiles(int64_t m, int64_t n, int64_t k, int sm_count) {
   };
   const int pairs = sm_count / 2;
   const Cand cands[] = {
-      {PersistentConfig::Pair256x256, 256, 256, pairs, kblock_clocks(128, 256, 256 * 128), false},
-      {PersistentConfig::Cta128x256, 128, 256, sm_count, kblock_clocks(128, 256, 384 * 128), false},
-      {PersistentConfig::Cta128x128, 128, 128, sm_count, kblock_clocks(128, 128, 256 * 128), false},
-      {PersistentConfig::SplitK256x256, 256, 256, sm_count, kblock_clocks(256, 256, 512 * 128), true},
-      {PersistentConfig::SplitK128x256, 128, 256, sm_count, kblock_clocks(128, 256, 384 * 128), true},
-      {PersistentConfig::SplitK128x128, 128, 128, sm_count, kblock_clocks(128, 128, 256 * 128), true},
+      {PersistentConfig::Pair256x256, 256, 256, pairs, 800.0, false},
+      {PersistentConfig::Cta128x256, 128, 256, sm_count, 870.0, false},
+      {PersistentConfig::Cta128x128, 128, 128, sm_count, 690.0, false},
+      {PersistentConfig::SplitK256x256, 256, 256, sm_count, 1000.0, true},
+      {PersistentConfig::SplitK128x256, 128, 256, sm_count, 570.0, true},
+      {PersistentConfig::SplitK128x128, 128, 128, sm_count, 570.0, true},
   };
   const char* forced = std::getenv("ZCUTLASS_SPLITK");
   const int forced_splits = forced != nullptr ? std::atoi(forced) : 0;
@@ -634,7 +627,7 @@ TileChoice choose_tiles(int64_t m, int64_t n, int64_t k, int sm_count) {
       if (forced_splits > 0) s = std::min<int64_t>(std::min<int64_t>(forced_splits, splitk::kMaxSplits), kb);
       if (s < 2) continue;
       splits = static_cast<int>(s);
-      cost = (double((kb + s - 1) / s) + 2.0) * c.per_kb;
+      cost = double((kb + s - 1) / s) * c.per_kb + 3000.0 + double(c.tile_m) * c.tile_n / 4.0;
     }
     if (cost < best_cost * 0.999) {
       best_cost = cost;
