@@ -67,7 +67,8 @@ FAMILIES = {
     "sk16": "_16x128x64_swapab_streamk",
     "sk32": "_32x128x64_swapab_streamk",
     "sk64": "_64x128x64_swapab_streamk",
-    "generic": "_generic",
+    "generic": "x32_generic",
+    "repack": "_repack_generic",
     "splitk256": "_128x256x64_splitk_cluster",
     "splitk128": "_128x128x64_splitk_cluster",
     "splitkm256": "_256x256x64_splitk_cluster",
@@ -93,6 +94,9 @@ FAMILY_SHAPES = {
     "splitkm256": [(256, 256, 64), (300, 520, 200), (256, 4096, 4096), (1000, 777, 1032), (129, 1024, 2048)],
     # odd leading dimensions (pads 3/5/7/11) on several 128 x 128 tiles, K tails of 1..31
     "generic": [(5, 7, 9), (100, 200, 50), (130, 70, 300), (1000, 777, 1032), (257, 1300, 2101)],
+    # the same odd layouts on the tcgen05 kernels through packed copies: the
+    # small-M (swap-AB), split-K and persistent routes
+    "repack": [(5, 7, 9), (60, 300, 200), (100, 200, 50), (257, 1300, 2101), (1000, 777, 1032), (2047, 3001, 1999)],
 }
 
 EPILOGUES = [  # (alpha, beta, bias)
@@ -119,7 +123,7 @@ def _family_params():
 def test_forced_family(cuda_device, monkeypatch, fam, shape, dt, col):
     monkeypatch.setenv("ZCUTLASS_FORCE_KERNEL", FAMILIES[fam])
     m, n, k = shape
-    if fam == "generic":
+    if fam in ("generic", "repack"):
         pads = (3, 5, 7, 11)
     else:
         # TMA families need leading dimensions that are multiples of 8 elements;

@@ -127,7 +127,7 @@ SelectDevice select_device() {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-enum class Kind { UmmaPair, UmmaPersistent, UmmaSplitK, UmmaSwapAb, UmmaSwapAbStreamK, Generic };
+enum class Kind { UmmaPair, UmmaPersistent, UmmaSplitK, UmmaSwapAb, UmmaSwapAbStreamK, Repack, Generic };
 
 class Sm100Operation final : public GemmOperation {
  public:
@@ -143,7 +143,7 @@ class Sm100Operation final : public GemmOperation {
     desc_.tile_n = tile_n;
     desc_.tile_k = tile_k;
     desc_.family = family;
-    desc_.requires_aligned_tiles = kind != Kind::Generic;
+    desc_.requires_aligned_tiles = kind != Kind::Generic && kind != Kind::Repack;
     desc_.supports_beta = true;
     desc_.supports_bias = true;
     // Stream-K decode: correct and deterministic, but its partial-tile fixup
@@ -166,6 +166,7 @@ class Sm100Operation final : public GemmOperation {
     if (desc_.experimental && !force_filter_active() && !experimental_allowed(desc_.name)) return false;
     const int64_t m = args.problem.m, n = args.problem.n, k = args.problem.k;
     if (kind_ == Kind::Generic) return true;
+    if (kind_ == Kind::Repack) return can_repack(args, m, n, k);
 
     // tcgen05 kernels: sm_100a code runs on compute capability 10.0 exactly.
     const SelectDevice dev = select_device();
@@ -209,7 +210,26 @@ class Sm100Operation final : public GemmOperation {
     }
   }
 
-  Status run(const GemmArguments& args, const GemmPreference&) const override {
+  // Packed-operand path: shapes large enough that one copy pass pays off
+  // (N, K >= 128, M*N*K >= 2^22) whose layout keeps the tcgen05 kernels out.
+  bool can_repack(const GemmArguments& args, int64_t m, int64_t n, int64_t k) const {
+    const SelectDevice dev = select_device();
+    if (dev.cc_major != 10 || dev.cc_minor != 0) return false;
+    if (m > INT_MAX || n > INT_MAX || k > INT_MAX) return false;
+    const zcb::LaunchArgs la = launch_args(args);
+    if (!force_filter_active()) {
+      if (n < 128 || k < 128 || m * n * k < (int64_t(1) << 22)) return false;
+      const bool small = m <= 64;
+      const bool regular = zcb::tma_compatible(la.a, la.lda) && zcb::tma_compatible(la.b, la.ldb) &&
+                           (small || (zcb::tma_compatible(la.d, la.ldd) &&
+                                      (la.c == nullptr || (aligned16(la.c) && (la.ldc & 7) == 0)) &&
+                                      (la.bias == nullptr || aligned16(la.bias))));
+      if (regular) return false;
+    }
+    return zcb::repack_ready_for_stream(zcb::repack_scratch_bytes(la), args.stream);
+  }
+
+  zcb::LaunchArgs launch_args(const GemmArguments& args) const {
     zcb::LaunchArgs la{};
     la.m = args.problem.m;
     la.n = args.problem.n;
@@ -228,6 +248,11 @@ class Sm100Operation final : public GemmOperation {
     la.bf16 = bf16_;
     la.b_col_major = args.B.layout == layout::LayoutKind::ColumnMajor;
     la.stream = args.stream;
+    return la;
+  }
+
+  Status run(const GemmArguments& args, const GemmPreference&) const override {
+    const zcb::LaunchArgs la = launch_args(args);
     cudaError_t e = cudaSuccess;
     switch (kind_) {
       case Kind::UmmaPair:
@@ -254,6 +279,9 @@ class Sm100Operation final : public GemmOperation {
       case Kind::UmmaSwapAb:
         e = zcb::launch_umma_swapab_gemm(la, nullptr);
         break;
+      case Kind::Repack:
+        e = zcb::launch_repack_gemm(la);
+        break;
       case Kind::Generic:
         e = zcb::launch_generic_gemm(la);
         break;
@@ -276,8 +304,9 @@ void register_builtin_operations() {
   // First match wins: small-M swap-AB buckets, then the cluster split-K and
   // persistent kernels (split-K 256x256 / 128x256 / 128x128, CTA-pair 256x256, or
   // one-CTA 128x256 / 128x128 tiles, whichever the cost model in
-  // choose_tiles picks), then the predicated CUDA-core kernel that accepts
-  // any layout.
+  // choose_tiles picks), then the same kernels on packed copies of operands
+  // TMA cannot describe, then the predicated CUDA-core kernel that accepts
+  // any layout (small problems, or a capture without scratch).
   static const Sm100Operation ops[] = {
       {"zcutlass_sm100_tcgen05_bf16_16x128x64_swapab_streamk", DType::BF16, K::UmmaSwapAbStreamK, 16, 128, 64, 12, F::Decode, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_f16_16x128x64_swapab_streamk", DType::F16, K::UmmaSwapAbStreamK, 16, 128, 64, 12, F::Decode, E::RegisterLinear},
@@ -303,6 +332,8 @@ void register_builtin_operations() {
       {"zcutlass_sm100_tcgen05_f16_128x256x64_ws_persistent", DType::F16, K::UmmaPersistent, 128, 256, 64, 4, F::Large, E::TmemRegisterTma},
       {"zcutlass_sm100_tcgen05_bf16_128x128x64_ws_persistent", DType::BF16, K::UmmaPersistent, 128, 128, 64, 6, F::Prefill, E::TmemRegisterTma},
       {"zcutlass_sm100_tcgen05_f16_128x128x64_ws_persistent", DType::F16, K::UmmaPersistent, 128, 128, 64, 6, F::Prefill, E::TmemRegisterTma},
+      {"zcutlass_sm100_tcgen05_bf16_repack_generic", DType::BF16, K::Repack, 128, 128, 64, 4, F::Fallback, E::RegisterLinear},
+      {"zcutlass_sm100_tcgen05_f16_repack_generic", DType::F16, K::Repack, 128, 128, 64, 4, F::Fallback, E::RegisterLinear},
       {"zcutlass_sm100_mma_bf16_128x128x32_generic", DType::BF16, K::Generic, 128, 128, 32, 2, F::Fallback, E::RegisterLinear},
       {"zcutlass_sm100_mma_f16_128x128x32_generic", DType::F16, K::Generic, 128, 128, 32, 2, F::Fallback, E::RegisterLinear},
   };

@@ -7,6 +7,7 @@
 #include <mutex>
 
 #include "kernels/generic_gemm.cuh"
+#include "kernels/repack.cuh"
 #include "kernels/sm100_umma_gemm.cuh"
 #include "kernels/sm100_umma_gemm_2cta.cuh"
 #include "kernels/sm100_umma_swapab.cuh"
@@ -764,6 +765,170 @@ cudaError_t launch_umma_swapab_gemm(const LaunchArgs& a, int* splits_used) {
 
 cudaError_t launch_generic_gemm(const LaunchArgs& a) {
   return a.bf16 ? launch_generic_t<__nv_bfloat16>(a) : launch_generic_t<half>(a);
+}
+
+// ---------------------------------------------------------------- generic path through packed operands
+//
+// Operands TMA cannot describe are copied once into 16-byte-aligned rows of a
+// per-(device, stream) scratch buffer, the tcgen05 kernels run on the packed
+// copies, and a packed D is copied out. The copies cost one pass over the
+// packed operands, against one pass per output tile for repacking inside the
+// GEMM's main loop.
+
+namespace {
+
+struct RepackScratch {
+  void* base = nullptr;
+  size_t bytes = 0;
+};
+std::mutex g_rp_mutex;
+std::map<std::pair<int, cudaStream_t>, RepackScratch> g_rp;
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+int64_t round8(int64_t x) { return (x + 7) & ~int64_t(7); }
+size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct RepackPlan {
+  bool small;  // M <= 64: the swap-AB kernels, which read C / bias and write D element by element
+  bool a, b, c, bias, d;
+  size_t off_a, off_b, off_c, off_bias, off_d, bytes;
+};
+
+RepackPlan plan_repack(const LaunchArgs& a) {
+  RepackPlan p{};
+  p.small = a.m <= 64;
+  p.a = !tma_compatible(a.a, a.lda);
+  p.b = !tma_compatible(a.b, a.ldb);
+  if (!p.small) {
+    p.c = a.c != nullptr && (!aligned16(a.c) || (a.ldc & 7) != 0);
+    p.bias = a.bias != nullptr && !aligned16(a.bias);
+    p.d = !tma_compatible(a.d, a.ldd);
+  }
+  size_t off = 0;
+  const auto take = [&off](bool used, size_t bytes) {
+    const size_t at = off;
+    if (used) off += round256(bytes);
+    return at;
+  };
+  p.off_a = take(p.a, size_t(a.m) * round8(a.k) * 2);
+  p.off_b = take(p.b, a.b_col_major ? size_t(a.n) * round8(a.k) * 2 : size_t(a.k) * round8(a.n) * 2);
+  p.off_c = take(p.c, size_t(a.m) * round8(a.n) * 2);
+  p.off_bias = take(p.bias, size_t(round8(a.n)) * 2);
+  p.off_d = take(p.d, size_t(a.m) * round8(a.n) * 2);
+  p.bytes = off;
+  return p;
+}
+
+cudaError_t launch_copy2d(void* dst, int64_t ld_dst, const void* src, int64_t ld_src, int64_t rows, int64_t cols,
+                          int64_t cols_out, int sm_count, cudaStream_t stream) {
+  const int64_t work = rows * ((cols_out + 7) / 8);
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((work + repack::kThreads - 1) / repack::kThreads,
+                                                                int64_t(sm_count) * 8));
+  repack::copy2d_u16_kernel<<<static_cast<unsigned>(blocks), repack::kThreads, 0, stream>>>(
+      static_cast<uint16_t*>(dst), ld_dst, static_cast<const uint16_t*>(src), ld_src, rows, cols, cols_out);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t repack_scratch_bytes(const LaunchArgs& a) { return plan_repack(a).bytes; }
+
+bool repack_ready_for_stream(size_t bytes, cudaStream_t stream) {
+  cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &status) != cudaSuccess) {
+    (void)cudaGetLastError();  // no device (host-only telemetry): not capturing
+    return true;
+  }
+  if (status == cudaStreamCaptureStatusNone) return true;
+  DeviceSlot* slot = current_slot();
+  if (slot == nullptr) return false;
+  std::lock_guard<std::mutex> lock(g_rp_mutex);
+  const auto it = g_rp.find({slot->info.ordinal, stream});
+  return it != g_rp.end() && it->second.bytes >= bytes;
+}
+
+cudaError_t launch_repack_gemm(const LaunchArgs& a) {
+  DeviceSlot* slot = current_slot();
+  if (slot == nullptr) return cudaErrorInvalidDevice;
+  const RepackPlan plan = plan_repack(a);
+  char* base = nullptr;
+  if (plan.bytes > 0) {
+    std::lock_guard<std::mutex> lock(g_rp_mutex);
+    RepackScratch& sc = g_rp[{slot->info.ordinal, a.stream}];
+    if (sc.bytes < plan.bytes) {
+      if (sc.base != nullptr) {
+        const cudaError_t e = cudaStreamSynchronize(a.stream);  // the old buffer may still be in use
+        if (e != cudaSuccess) return e;
+        cudaFree(sc.base);
+        sc = RepackScratch{};
+      }
+      const size_t want = std::max<size_t>(plan.bytes, size_t(16) << 20);
+      const cudaError_t e = cudaMalloc(&sc.base, want);
+      if (e != cudaSuccess) return e;
+      sc.bytes = want;
+    }
+    base = static_cast<char*>(sc.base);
+  }
+  const int sms = slot->info.sm_count;
+  LaunchArgs b = a;
+  cudaError_t e = cudaSuccess;
+  if (plan.a) {
+    b.a = base + plan.off_a;
+    b.lda = round8(a.k);
+    e = launch_copy2d(base + plan.off_a, b.lda, a.a, a.lda, a.m, a.k, b.lda, sms, a.stream);
+    if (e != cudaSuccess) return e;
+  }
+  if (plan.b) {
+    const int64_t rows = a.b_col_major ? a.n : a.k, cols = a.b_col_major ? a.k : a.n;
+    b.b = base + plan.off_b;
+    b.ldb = round8(cols);
+    e = launch_copy2d(base + plan.off_b, b.ldb, a.b, a.ldb, rows, cols, b.ldb, sms, a.stream);
+    if (e != cudaSuccess) return e;
+  }
+  if (plan.c) {
+    b.c = base + plan.off_c;
+    b.ldc = round8(a.n);
+    e = launch_copy2d(base + plan.off_c, b.ldc, a.c, a.ldc, a.m, a.n, b.ldc, sms, a.stream);
+    if (e != cudaSuccess) return e;
+  }
+  if (plan.bias) {
+    b.bias = base + plan.off_bias;
+    e = launch_copy2d(base + plan.off_bias, 0, a.bias, 0, 1, a.n, round8(a.n), sms, a.stream);
+    if (e != cudaSuccess) return e;
+  }
+  if (plan.d) {
+    b.d = base + plan.off_d;
+    b.ldd = round8(a.n);
+  }
+  if (plan.small) {
+    e = launch_umma_swapab_gemm(b, nullptr);
+  } else {
+    const TileChoice tc = choose_tiles(a.m, a.n, a.k, sms);
+    switch (tc.config) {
+      case PersistentConfig::Pair256x256:
+        e = launch_umma_pair_gemm(b);
+        break;
+      case PersistentConfig::Cta128x256:
+        e = launch_umma_gemm(b, 256);
+        break;
+      case PersistentConfig::Cta128x128:
+        e = launch_umma_gemm(b, 128);
+        break;
+      case PersistentConfig::SplitK256x256:
+        e = launch_umma_splitk_gemm(b, 256, 256, tc.splits);
+        break;
+      case PersistentConfig::SplitK128x256:
+        e = launch_umma_splitk_gemm(b, 128, 256, tc.splits);
+        break;
+      case PersistentConfig::SplitK128x128:
+        e = launch_umma_splitk_gemm(b, 128, 128, tc.splits);
+        break;
+    }
+  }
+  if (e != cudaSuccess) return e;
+  if (plan.d) e = launch_copy2d(a.d, a.ldd, b.d, b.ldd, a.m, a.n, a.n, sms, a.stream);
+  return e;
 }
 
 int read_and_clear_error_word(bool clear) {

@@ -61,6 +61,15 @@ bool swapab_prefer_streamk(int64_t n, int64_t k, int sm_count);
 bool swapab_sk_ready_for_stream(int64_t m, int64_t n, int64_t k, cudaStream_t stream);
 // Predicated CUDA-core kernel for TMA-incompatible layouts.
 cudaError_t launch_generic_gemm(const LaunchArgs& args);
+// TMA-incompatible layouts on the tcgen05 kernels: the operands TMA cannot
+// describe (and C, bias, D where the chosen kernel needs them aligned) are
+// copied into 16-byte-aligned rows of a per-(device, stream) scratch buffer
+// owned by the library, grown on first use.
+cudaError_t launch_repack_gemm(const LaunchArgs& args);
+size_t repack_scratch_bytes(const LaunchArgs& args);
+// False only while `stream` is being captured into a CUDA graph and its
+// scratch buffer does not yet hold `bytes` (allocation is not allowed then).
+bool repack_ready_for_stream(size_t bytes, cudaStream_t stream);
 
 // Cluster split-K tcgen05 kernel, one bm x bn tile (128 x 128, 128 x 256 or
 // 256 x 256) per cluster of `splits` CTAs along K, reduced through distributed
