@@ -324,3 +324,46 @@ def test_gemm_gather_a(cuda_device, m, n, k, parts, alpha, beta, bias):
     assert _native.device_error(clear=True) == 0
     out = oracle.bits_to_float(to_host(dd), BF16)
     oracle.check(out, ref, BF16)
+
+
+@pytest.mark.gpu
+def test_repack_path_in_cuda_graph(cuda_device):
+    """The packed-operand path replayed from a CUDA graph equals its eager
+    result bit for bit; a capture on a stream that has no scratch buffer yet is
+    served by the predicated kernel instead (no allocation while capturing)."""
+    import torch
+
+    m, n, k = 300, 1000, 1031  # K odd: A and B cannot be described by TMA
+    g0 = torch.Generator(device="cpu").manual_seed(9)
+    a = torch.randn(m, k, generator=g0).to(torch.bfloat16).cuda()
+    b = (torch.randn(k, n, generator=g0) / k ** 0.5).to(torch.bfloat16).cuda()
+    s = torch.cuda.Stream()
+    desc = _native.make_desc(m, n, k, k, n, n, n, BF16, stream=s.cuda_stream)
+    assert "repack_generic" in _native.selected_kernel(desc)["kernel_name"]
+    ref = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    with torch.cuda.stream(s):
+        assert _native.gemm(desc, a.data_ptr(), b.data_ptr(), None, ref.data_ptr()) == 0  # sizes the scratch
+    torch.cuda.synchronize()
+    d = torch.empty_like(ref)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        desc.stream = torch.cuda.current_stream().cuda_stream
+        assert _native.gemm(desc, a.data_ptr(), b.data_ptr(), None, d.data_ptr()) == 0
+    for _ in range(2):
+        d.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(d, ref)
+    del g
+    # a fresh stream has no scratch: the capture takes the predicated kernel
+    s2 = torch.cuda.Stream()
+    d2 = torch.empty_like(ref)
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2, stream=s2):
+        desc.stream = torch.cuda.current_stream().cuda_stream
+        assert _native.gemm(desc, a.data_ptr(), b.data_ptr(), None, d2.data_ptr()) == 0
+    g2.replay()
+    torch.cuda.synchronize()
+    rel = float((d2.float() - ref.float()).norm() / ref.float().norm())
+    assert rel < 5e-3, rel
+    assert _native.device_error(clear=True) == 0

@@ -343,6 +343,7 @@ void run_shape(const Shape& s, const Options& o, cublasHandle_t handle, const cu
   if (stream != nullptr) {
     CHECK_CUBLAS(cublasSetStream(handle, nullptr));
     CHECK_CUDA(cudaStreamDestroy(stream));
+    desc.stream = nullptr;  // the telemetry below must not see the destroyed stream
   }
   const double flops = 2.0 * double(s.m) * s.n * s.k;
   const double z_tf = z_ms > 0 ? flops / (z_ms * 1e-3) / 1e12 : 0.0;

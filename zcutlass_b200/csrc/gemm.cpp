@@ -345,10 +345,14 @@ void ensure_registered() { std::call_once(g_register_once, register_builtin_oper
 
 const void* const kDummy = reinterpret_cast<const void*>(uintptr_t(256));
 
+// Telemetry answers for the descriptor's shape, types and layouts only: the
+// selection runs as for a call outside any stream capture, and never passes
+// desc.stream to the CUDA runtime (a descriptor may outlive its stream).
 const GemmOperationDescription* select_description(const GemmDesc& desc) {
   ensure_registered();
-  const GemmArguments args = make_arguments(desc, kDummy, kDummy, desc.beta != 0.0f ? kDummy : nullptr,
-                                            const_cast<void*>(kDummy));
+  GemmArguments args = make_arguments(desc, kDummy, kDummy, desc.beta != 0.0f ? kDummy : nullptr,
+                                      const_cast<void*>(kDummy));
+  args.stream = nullptr;
   const GemmOperation* op = gemm_api::global_manifest().find_best(args, {});
   return op != nullptr ? &op->description() : nullptr;
 }
