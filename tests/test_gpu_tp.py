@@ -64,3 +64,22 @@ def test_bench_two_gpus_exits(comm):
     line = json.loads(lines[0])
     assert line["n_gpus"] == 2 and line["value"] > 0 and line["e2e"]["value"] > 0
     assert "teardown did not finish" not in r.stderr
+
+
+@pytest.mark.gpu
+def test_vllm_tensor_parallel_native_weight(tmp_path):
+    """vLLM's Column/RowParallelLinear with the zcutlass LinearMethod on native
+    [N, K] weight shards, the all-reduce left to vLLM, against the oracle
+    (tests/vllm_tp_worker.py)."""
+    pytest.importorskip("vllm.model_executor.layers.linear")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 or more GPUs")
+    report = tmp_path / "vllm_tp.json"
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           str(ROOT / "tests" / "vllm_tp_worker.py"), str(report)]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=420, cwd=ROOT, env=dict(os.environ))
+    assert r.returncode == 0, f"stdout:\n{r.stdout[-3000:]}\nstderr:\n{r.stderr[-6000:]}"
+    rep = json.loads(report.read_text())
+    assert rep["world"] == 2 and rep["weight_cache"] == "native"
+    assert rep["row"]["bound_ratio"] <= 1.0
