@@ -152,8 +152,11 @@ def check_layer_overlap(tp: TPGroup, dev, use_nvls: bool) -> dict:
 def check_sequence_parallel(tp: TPGroup, dev) -> dict:
     """The sequence-parallel step (reduce-scatters, and qkv / gate_up reading
     their A rows from the owning ranks inside the GEMM) gives this rank's rows
-    of the all-reduce step's output; two overlapped lanes and a CUDA graph
-    replay give the same bits."""
+    of the all-reduce step's output within the BF16 product tolerance (the
+    all-reduce step may run these mid-M GEMMs as cluster split-K, whose
+    partial sums round differently from the gathered persistent kernel's
+    single accumulator); two overlapped lanes and a CUDA graph replay give the
+    sequence-parallel step's own bits."""
     shape = LayerShape(hidden=1024, intermediate=2048, q_heads=8, kv_heads=2, head_dim=128)
     layer = TPDecoderLinears(shape, tp, dev, torch.bfloat16, seed=4, chunks=2)
     rows = 256 * tp.world_size
@@ -170,7 +173,7 @@ def check_sequence_parallel(tp: TPGroup, dev) -> dict:
     torch.cuda.synchronize(dev)
     exact = float((y == ref[r0:r1]).float().mean())
     rel = float((y.float() - ref[r0:r1].float()).norm() / ref[r0:r1].float().norm())
-    assert rel < 1e-3, f"sequence-parallel vs all-reduce step: rel {rel}"
+    assert rel < 5e-3, f"sequence-parallel vs all-reduce step: rel {rel}"
     streams = [torch.cuda.Stream(dev) for _ in range(2)]
     for _ in range(3):
         ys = [t[r0:r1].clone() for t in layer.forward_sp_overlapped(rows, streams)]
