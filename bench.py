@@ -11,8 +11,9 @@ all-reduce of the BF16 partials: the library's NVLS kernel, or NCCL with
 blocks on two streams (--micro), so one block's all-reduce overlaps the other
 block's GEMMs. 3573 GFLOP per step for the whole job, whatever the rank
 count (strong scaling). --sp 1 runs the sequence-parallel form of the same
-step instead (reduce-scatters, with qkv / gate_up reading the other ranks'
-rows inside the GEMM; NVLS only).
+step instead (reduce-scatters; qkv / gate_up get the other ranks' rows by
+copy-engine copies into local memory, or inside the GEMM with --sp-gather
+fused; NVLS only).
 
     python bench.py                          # N=1, defaults
     torchrun --nproc-per-node N bench.py --gpus N --steps K --warmup W
@@ -349,14 +350,16 @@ def run_gpu(args) -> int:
     micro = args.micro if args.micro > 0 else (2 if world > 1 else 1)
     comm = "none"
     if world > 1:
-        want_nvls = args.comm == "nvls" or (args.comm == "auto" and world >= 4)
+        want_nvls = args.comm in ("nvls", "auto")
         comm = "nvls" if want_nvls and layer.enable_nvls(TOKENS, lanes=micro) else "nccl"
     streams = [torch.cuda.Stream(device) for _ in range(micro)] if micro > 1 else None
     args.micro_used = micro
     lane_rows = TOKENS // micro
     # sequence-parallel layer: activations row-sharded between the linears,
-    # reduce-scatters instead of all-reduces, the gathers fused into the GEMMs
+    # reduce-scatters instead of all-reduces, peer row blocks copied in (or
+    # read inside the GEMMs with --sp-gather fused)
     sp = bool(args.sp) and comm == "nvls" and TOKENS % micro == 0 and layer.enable_sequence_parallel(TOKENS, micro)
+    layer.sp_gather = args.sp_gather
     g = torch.Generator(device="cpu").manual_seed(1)
     x_host = torch.randn(TOKENS, LLAMA3_8B.hidden, generator=g).to(torch.bfloat16)
     x = x_host.to(device)
@@ -475,7 +478,7 @@ def run_gpu(args) -> int:
                "allreduce": {"nvls": "zcutlass_nvls_allreduce (multimem.ld_reduce acc::f32 + multimem.st)",
                              "nccl": f"NCCL all_reduce, {args.chunks} row chunks", "none": "none (TP1)"}[comm],
                "micro_batches": micro, "cuda_graph": use_graph,
-               "sequence_parallel": sp,
+               "sequence_parallel": sp, **({"sp_gather": args.sp_gather} if sp else {}),
                "order": "qkv -> o_proj (+all-reduce) -> gate_up -> down (+all-reduce)"}
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
@@ -712,9 +715,12 @@ def main(argv=None) -> int:
                     help="replay each step from a CUDA graph (auto: when TP > 1)")
     ap.add_argument("--sp", type=int, default=0,
                     help="1: sequence-parallel layer (reduce-scatters, all-gathers fused into the GEMMs; NVLS only)")
+    ap.add_argument("--sp-gather", choices=["copy", "fused"], default="copy",
+                    help="--sp 1: peer row blocks copied into local memory by the copy engines before a plain GEMM "
+                         "(copy), or read from the owners inside the GEMM (fused)")
     ap.add_argument("--comm", choices=["auto", "nvls", "nccl"], default="auto",
-                    help="row-parallel all-reduce: the library's NVLS kernel or NCCL (auto: NVLS from TP4 up; "
-                         "at TP2 NVLS moves 1.5x the bytes of a ring and NCCL is faster)")
+                    help="row-parallel all-reduce: the library's NVLS kernel or NCCL (auto: NVLS where the "
+                         "GPUs support multicast, else NCCL; measured faster than NCCL at TP2 and TP8)")
     ap.add_argument("--skip-decode", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     args = ap.parse_args(argv)

@@ -150,13 +150,16 @@ def check_layer_overlap(tp: TPGroup, dev, use_nvls: bool) -> dict:
 
 
 def check_sequence_parallel(tp: TPGroup, dev) -> dict:
-    """The sequence-parallel step (reduce-scatters, and qkv / gate_up reading
-    their A rows from the owning ranks inside the GEMM) gives this rank's rows
-    of the all-reduce step's output within the BF16 product tolerance (the
-    all-reduce step may run these mid-M GEMMs as cluster split-K, whose
-    partial sums round differently from the gathered persistent kernel's
-    single accumulator); two overlapped lanes and a CUDA graph replay give the
-    sequence-parallel step's own bits."""
+    """The sequence-parallel step (reduce-scatters, qkv / gate_up on the other
+    ranks' rows) gives this rank's rows of the all-reduce step's output, for
+    both ways of getting those rows:
+      * "copy" (peer row blocks copied into local memory, then the same GEMMs
+        as the all-reduce step): bit for bit;
+      * "fused" (rows read from the owners inside the GEMM): within the BF16
+        product tolerance -- the all-reduce step may run these mid-M GEMMs as
+        cluster split-K, whose partial sums round differently from the
+        gathered persistent kernel's single accumulator.
+    Two overlapped lanes and a CUDA graph replay give the step's own bits."""
     shape = LayerShape(hidden=1024, intermediate=2048, q_heads=8, kv_heads=2, head_dim=128)
     layer = TPDecoderLinears(shape, tp, dev, torch.bfloat16, seed=4, chunks=2)
     rows = 256 * tp.world_size
@@ -169,26 +172,32 @@ def check_sequence_parallel(tp: TPGroup, dev) -> dict:
     dist.barrier()
     ref = layer.forward(x).clone()  # all-reduce path
     r0, r1 = shard_range(rows, tp.rank, tp.world_size)
-    y = layer.forward_sp(rows)[r0:r1].clone()
-    torch.cuda.synchronize(dev)
-    exact = float((y == ref[r0:r1]).float().mean())
-    rel = float((y.float() - ref[r0:r1].float()).norm() / ref[r0:r1].float().norm())
-    assert rel < 5e-3, f"sequence-parallel vs all-reduce step: rel {rel}"
     streams = [torch.cuda.Stream(dev) for _ in range(2)]
-    for _ in range(3):
-        ys = [t[r0:r1].clone() for t in layer.forward_sp_overlapped(rows, streams)]
+    report = {}
+    for mode in ("copy", "fused"):
+        layer.sp_gather = mode
+        y = layer.forward_sp(rows)[r0:r1].clone()
         torch.cuda.synchronize(dev)
-        assert all(torch.equal(t, y) for t in ys), "overlapped sequence-parallel lanes differ"
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, capture_error_mode="thread_local"):
-        outs = layer.forward_sp_overlapped(rows, streams)
-    for _ in range(3):
-        graph.replay()
-        torch.cuda.synchronize(dev)
-        assert all(torch.equal(t[r0:r1], y) for t in outs), "graph replay of the sequence-parallel step differs"
-    del graph
-    assert _native.device_error(True) == 0
-    return {"exact_fraction_vs_allreduce": exact, "rel_frobenius": rel}
+        exact = float((y == ref[r0:r1]).float().mean())
+        rel = float((y.float() - ref[r0:r1].float()).norm() / ref[r0:r1].float().norm())
+        if mode == "copy":
+            assert exact == 1.0, f"sequence-parallel (copy) vs all-reduce step: exact fraction {exact}, rel {rel}"
+        assert rel < 5e-3, f"sequence-parallel ({mode}) vs all-reduce step: rel {rel}"
+        for _ in range(3):
+            ys = [t[r0:r1].clone() for t in layer.forward_sp_overlapped(rows, streams)]
+            torch.cuda.synchronize(dev)
+            assert all(torch.equal(t, y) for t in ys), f"overlapped sequence-parallel lanes differ ({mode})"
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+            outs = layer.forward_sp_overlapped(rows, streams)
+        for _ in range(3):
+            graph.replay()
+            torch.cuda.synchronize(dev)
+            assert all(torch.equal(t[r0:r1], y) for t in outs), f"graph replay of the sequence-parallel step differs ({mode})"
+        del graph
+        assert _native.device_error(True) == 0
+        report[mode] = {"exact_fraction_vs_allreduce": exact, "rel_frobenius": rel}
+    return report
 
 
 def main() -> None:

@@ -171,6 +171,8 @@ class NvlsReducer:
         self.raw = raw
         self.bufs = [raw[i * region: i * region + max_rows * cols * elem].view(dtype).view(max_rows, cols)
                      for i in range(nbufs)]
+        self._region_elems = region // elem
+        self._peer_views: dict = {}
         # multicast address = multicast base + offset of the local address in the allocation
         self.mc_base = self.handle.multicast_ptr - self.handle.buffer_ptrs[self.rank]
         self.flag = raw.data_ptr() + nbufs * region
@@ -199,6 +201,32 @@ class NvlsReducer:
         """Address of buffer i in every rank's allocation (peer-mapped), by rank."""
         off = self.bufs[i].data_ptr() - self.handle.buffer_ptrs[self.rank]
         return [int(base) + off for base in self.handle.buffer_ptrs]
+
+    def peer_view(self, r: int, i: int):
+        """Buffer i of rank r's allocation as a tensor mapped into this GPU's
+        address space (reads and writes cross NVLink)."""
+        key = (r, i)
+        if key not in self._peer_views:
+            rows, cols = self.bufs[i].shape
+            self._peer_views[key] = self.handle.get_buffer(r, (rows, cols), self.dtype,
+                                                           storage_offset=i * self._region_elems)
+        return self._peer_views[key]
+
+    def gather_rows(self, i: int, rows: int) -> None:
+        """Copies every other rank's published row block of buffer i
+        (rows [r * rows / W, (r + 1) * rows / W) of rank r's copy) into the
+        same rows of this rank's copy, one device-to-device copy per rank on
+        the current stream: the copy engines move them over NVLink, once, and
+        no SM is used. Call after the reduce-scatter that published them
+        (its closing barrier orders every rank's stores before these reads);
+        the rows overwritten here held this rank's partials for the other
+        blocks, which every peer finished reading before that barrier."""
+        mine = self.bufs[i]
+        for r in range(self.world):
+            if r == self.rank:
+                continue
+            lo, hi = shard_range(rows, r, self.world)
+            mine[lo:hi].copy_(self.peer_view(r, i)[lo:hi])
 
     def _code(self):
         import torch
@@ -400,6 +428,12 @@ class TPDecoderLinears:
         self.d_cols = d_hi - d_lo
         self._bufs = {}
         self.sp_inputs: list[NvlsReducer] = []  # set by enable_sequence_parallel()
+        # How qkv / gate_up see the other ranks' rows in the sequence-parallel
+        # step: "copy" brings each peer row block into local memory once (copy
+        # engines) and runs the plain GEMM; "fused" reads them inside the GEMM
+        # (zcutlass_gemm_gather_a), which re-reads each remote A tile once per
+        # N tile.
+        self.sp_gather = "copy"
 
     def enable_nvls(self, max_tokens: int, lanes: int = 1) -> bool:
         """Use the library's NVLS all-reduce for both row-parallel linears."""
@@ -427,9 +461,10 @@ class TPDecoderLinears:
         callables (through o_proj's reduce-scatter, then the rest). Rank r owns
         rows [r * rows / W, (r + 1) * rows / W) of the block: its input rows
         sit in buffer xi of the lane's input set, and it ends with the same
-        rows of the down output (the sum over ranks). qkv and gate_up read
-        the other ranks' rows straight from their buffers inside the GEMM;
-        o_proj and down end in an NVLS reduce-scatter."""
+        rows of the down output (the sum over ranks). qkv and gate_up get the
+        other ranks' rows as `sp_gather` says (copied into this rank's buffer,
+        or read from the owners' buffers inside the GEMM); o_proj and down end
+        in an NVLS reduce-scatter."""
         b = self.buffers(rows, self.qkv.weight.device, self.qkv.weight.dtype, lane)
         x_in = self.sp_inputs[lane]
         state = {}
@@ -456,13 +491,20 @@ class TPDecoderLinears:
             red.reduce_scatter(i, rows)
             state["y"] = y
 
+        def gathered(col: ColumnParallelLinear, red: NvlsReducer, i: int, out):
+            if self.sp_gather == "fused":
+                col.forward_gathered(red.peer_ptrs(i), rows, out)
+            else:
+                red.gather_rows(i, rows)
+                col.forward(red.bufs[i][:rows], out=out)
+
         def first():
-            timed("qkv", lambda: self.qkv.forward_gathered(x_in.peer_ptrs(xi), rows, b["qkv"]))
+            timed("qkv", lambda: gathered(self.qkv, x_in, xi, b["qkv"]))
             timed("o_proj", o_proj)
 
         def second():
             red, i = state["o"]
-            timed("gate_up", lambda: self.gate_up.forward_gathered(red.peer_ptrs(i), rows, b["gate_up"]))
+            timed("gate_up", lambda: gathered(self.gate_up, red, i, b["gate_up"]))
             timed("down", down)
 
         return first, second, state
