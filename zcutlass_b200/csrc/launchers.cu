@@ -586,30 +586,34 @@ const DeviceInfo* current_device_info() {
 }
 
 TileChoice choose_tiles(int64_t m, int64_t n, int64_t k, int sm_count) {
-  // Time model in SM clocks, calibrated on B200 from per-CTA phase timestamps
-  // and graph-timed runs (bf16, 148 SMs):
-  //   persistent: waves x K blocks x clocks per K block of one tile
-  //     (CTA pair 256x256: 800, 128x256: 870, 128x128: 690);
-  //   split-K (one wave): ceil(K blocks / S) x clocks per K block (128-row
-  //     tiles 570, 256x256: 1000) + the cross-CTA reduction, which moves the
-  //     whole FP32 partial through distributed shared memory: 3000 + BM*BN/4.
-  // The model reproduces the measured order of the configurations on 256 x
-  // {1024..8192}^2, 512 / 1024 x 4096^2, 2048 x 1536^2 and 8192 x 28672 x 4096.
+  // Time model in SM clocks, fitted on B200 to graph-timed runs (bf16, 148
+  // SMs, B column-major, weights rotated past L2) of every configuration on
+  // M x N x K = 64 / 128 / 256 / 512 / 1024 x 4096^2, 256 x 8192^2,
+  // 256 x 1536^2, 256 x 2048 x 1536, 256 x 14336 x 4096, 1024^3 and
+  // 8192 x 28672 x 4096:
+  //   persistent: waves x K blocks x clocks per K block of one tile + fixed
+  //     (CTA pair 256x256: 800 + 5000, 128x256: 820 + 7000, 128x128: 600 + 9000);
+  //   split-K (one wave): ceil(K blocks / S) x clocks per K block + fixed,
+  //     the fixed part being mostly the cross-CTA reduction of the FP32
+  //     partial through distributed shared memory (128x128: 645 + 12600,
+  //     128x256: 990 + 15500, 256x256: 1450 + 40000).
+  // It picks the fastest measured configuration on each of those shapes
+  // (within 3 %).
   const int64_t kb = (k + 63) / 64;
   struct Cand {
     PersistentConfig cfg;
     int tile_m, tile_n, units;  // units: CTAs (or CTA pairs) resident at once
-    double per_kb;
+    double per_kb, fixed;
     bool split;
   };
   const int pairs = sm_count / 2;
   const Cand cands[] = {
-      {PersistentConfig::Pair256x256, 256, 256, pairs, 800.0, false},
-      {PersistentConfig::Cta128x256, 128, 256, sm_count, 870.0, false},
-      {PersistentConfig::Cta128x128, 128, 128, sm_count, 690.0, false},
-      {PersistentConfig::SplitK256x256, 256, 256, sm_count, 1000.0, true},
-      {PersistentConfig::SplitK128x256, 128, 256, sm_count, 570.0, true},
-      {PersistentConfig::SplitK128x128, 128, 128, sm_count, 570.0, true},
+      {PersistentConfig::Pair256x256, 256, 256, pairs, 800.0, 5000.0, false},
+      {PersistentConfig::Cta128x256, 128, 256, sm_count, 820.0, 7000.0, false},
+      {PersistentConfig::Cta128x128, 128, 128, sm_count, 600.0, 9000.0, false},
+      {PersistentConfig::SplitK256x256, 256, 256, sm_count, 1450.0, 40000.0, true},
+      {PersistentConfig::SplitK128x256, 128, 256, sm_count, 990.0, 15500.0, true},
+      {PersistentConfig::SplitK128x128, 128, 128, sm_count, 645.0, 12600.0, true},
   };
   const char* forced = std::getenv("ZCUTLASS_SPLITK");
   const int forced_splits = forced != nullptr ? std::atoi(forced) : 0;
@@ -621,14 +625,14 @@ TileChoice choose_tiles(int64_t m, int64_t n, int64_t k, int sm_count) {
     double cost;
     int splits = 1;
     if (!c.split) {
-      cost = double((tiles + c.units - 1) / c.units) * double(kb) * c.per_kb;
+      cost = double((tiles + c.units - 1) / c.units) * double(kb) * c.per_kb + c.fixed;
     } else {
       if (tiles * 2 > sm_count) continue;  // split-K only when the tiles alone leave SMs idle
       int64_t s = std::min<int64_t>({int64_t(splitk::kMaxSplits), sm_count / tiles, kb / 2});
       if (forced_splits > 0) s = std::min<int64_t>(std::min<int64_t>(forced_splits, splitk::kMaxSplits), kb);
       if (s < 2) continue;
       splits = static_cast<int>(s);
-      cost = double((kb + s - 1) / s) * c.per_kb + 3000.0 + double(c.tile_m) * c.tile_n / 4.0;
+      cost = double((kb + s - 1) / s) * c.per_kb + c.fixed;
     }
     if (cost < best_cost * 0.999) {
       best_cost = cost;
