@@ -10,10 +10,12 @@
 // enough loads in flight it splits K across the CTAs of a thread-block cluster
 // (cluster = splits x 1 x 1, all working on the same 128-column slice of N).
 // Each CTA parks its FP32 partial in its own shared memory, the cluster
-// synchronises, and CTA r reduces rows [r*128/S, (r+1)*128/S) by reading every
-// peer's partial through distributed shared memory (ld.shared::cluster), then
-// applies alpha/beta/bias and writes D with coalesced stores. No global
-// scratch memory is used.
+// synchronises, and CTA r reduces its share of the tile's 32 groups of 4
+// rows of D^T (groups [r*32/S, (r+1)*32/S)) by reading every peer's partial
+// through distributed shared memory (ld.shared::cluster.v4, all CTAs' loads of
+// a pass in flight at once: the remote-load latency is paid once per pass,
+// and one pass covers M <= 16), then applies alpha/beta/bias and writes D
+// with coalesced stores. No global scratch memory is used.
 #pragma once
 
 #include "sm100_ptx.cuh"
@@ -39,7 +41,7 @@ constexpr int kBlockN = 128;  // rows of D^T per CTA (MMA M)
 constexpr int kBlockK = 64;   // one 128-byte swizzle row of K; a stage holds KSUB of them
 constexpr int kThreads = 192;
 constexpr int kMaxSplits = 8;  // cluster size limit (portable)
-constexpr int kRedUnroll = 4;  // reduction elements per thread per pass
+constexpr int kRedUnroll = 2;  // reduction groups (4 outputs each) per thread per pass
 
 // A pipeline stage holds KSUB K sub-blocks of 64: TMA streams a weight
 // matrix at ~4.7 TB/s with 16 KiB per stage but ~5.7 TB/s with >= 32 KiB
@@ -70,9 +72,12 @@ enum : int {
   kErrEpiTmemFull = (7 << 4) | 3,
 };
 
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(map_shared_rank(local_addr, rank)) : "memory");
+__device__ __forceinline__ float4 ld_dsmem_v4f(uint32_t local_addr, uint32_t rank) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(map_shared_rank(local_addr, rank))
+               : "memory");
   return v;
 }
 
@@ -235,47 +240,58 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
   cluster_sync_all();
 
-  if (warp >= 2) {
+  {
     const T* cptr = static_cast<const T*>(p.c);
     const T* bptr = static_cast<const T*>(p.bias);
     T* dptr = static_cast<T*>(p.d);
     const bool has_c = (p.epi_flags & kEpiHasC) != 0;
     const bool has_bias = (p.epi_flags & kEpiHasBias) != 0;
-    const int r_begin = static_cast<int>((split * kBlockN) / p.splits);
-    const int r_end = static_cast<int>(((split + 1) * kBlockN) / p.splits);
-    const int rows = r_end - r_begin;
-    const int tid = threadIdx.x - 64;
+    constexpr int kGroups = kBlockN / 4;  // groups of 4 rows of D^T (4 consecutive n)
+    const int g_begin = static_cast<int>((split * kGroups) / p.splits);
+    const int g_end = static_cast<int>(((split + 1) * kGroups) / p.splits);
+    const int groups = g_end - g_begin;
     const uint32_t red_addr = smem_addr(red);
-    const int total = rows * p.m;
-    // kRedUnroll elements per thread per pass, every remote load of the pass
-    // issued before the first sum: the DSMEM latency is paid once per pass.
+    const int total = groups * p.m;  // work items: (token mi, group g)
+    // Every thread of the CTA takes kRedUnroll items per pass, every remote
+    // load of the pass issued before the first sum.
 #pragma unroll 1
-    for (int i0 = tid; i0 < total; i0 += 128 * kRedUnroll) {
-      float part[kRedUnroll][kMaxSplits];
+    for (int i0 = threadIdx.x; i0 < total; i0 += kThreads * kRedUnroll) {
+      float4 part[kRedUnroll][kMaxSplits];
 #pragma unroll
       for (int u = 0; u < kRedUnroll; ++u) {
-        const int idx = i0 + u * 128;
+        const int idx = i0 + u * kThreads;
         if (idx >= total) continue;
-        const uint32_t off = static_cast<uint32_t>(((idx / rows) * kBlockN + r_begin + idx % rows) * 4);
+        const uint32_t off = static_cast<uint32_t>(((idx / groups) * kBlockN + 4 * (g_begin + idx % groups)) * 4);
 #pragma unroll
         for (int s = 0; s < kMaxSplits; ++s)
-          part[u][s] = s < p.splits ? ld_dsmem_f32(red_addr + off, static_cast<uint32_t>(s)) : 0.0f;
+          if (s < p.splits) part[u][s] = ld_dsmem_v4f(red_addr + off, static_cast<uint32_t>(s));
       }
 #pragma unroll
       for (int u = 0; u < kRedUnroll; ++u) {
-        const int idx = i0 + u * 128;
+        const int idx = i0 + u * kThreads;
         if (idx >= total) continue;
-        const int mi = idx / rows;
-        const int n = n0 + r_begin + idx % rows;
-        if (n >= p.n) continue;
-        float sum = 0.0f;  // in split order: the result does not depend on timing
+        const int mi = idx / groups;
+        const int nb = n0 + 4 * (g_begin + idx % groups);
+        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);  // in split order: the result does not depend on timing
 #pragma unroll
-        for (int s = 0; s < kMaxSplits; ++s)
-          if (s < p.splits) sum += part[u][s];
-        float v = p.alpha * sum;
-        if (has_c) v += p.beta * Elem<T>::to_float(cptr[static_cast<int64_t>(mi) * p.ldc + n]);
-        if (has_bias) v += Elem<T>::to_float(bptr[n]);
-        dptr[static_cast<int64_t>(mi) * p.ldd + n] = Elem<T>::from_float(v);
+        for (int s = 0; s < kMaxSplits; ++s) {
+          if (s < p.splits) {
+            sum.x += part[u][s].x;
+            sum.y += part[u][s].y;
+            sum.z += part[u][s].z;
+            sum.w += part[u][s].w;
+          }
+        }
+        const float v4[4] = {sum.x, sum.y, sum.z, sum.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int n = nb + j;
+          if (n >= p.n) continue;
+          float v = p.alpha * v4[j];
+          if (has_c) v += p.beta * Elem<T>::to_float(cptr[static_cast<int64_t>(mi) * p.ldc + n]);
+          if (has_bias) v += Elem<T>::to_float(bptr[n]);
+          dptr[static_cast<int64_t>(mi) * p.ldd + n] = Elem<T>::from_float(v);
+        }
       }
     }
   }
