@@ -63,9 +63,12 @@ def main() -> None:
         wc = oracle.make_tensor(n, k, k, 32, F16)  # column-parallel weight [N, K]
         bc = oracle.make_tensor(1, n, n, 33, F16)[0]
         wr = oracle.make_tensor(k, n, n, 34, F16)  # row-parallel weight [K_out = k, K_in = n]
-        col = ColumnParallelLinear(k, n, bias=True, params_dtype=torch.float16,
-                                   prefix="model.layers.0.self_attn.qkv_proj")
-        row = RowParallelLinear(n, k, bias=False, params_dtype=torch.float16, prefix="model.layers.0.self_attn.o_proj")
+        with torch.device(dev):  # as vLLM's model loader does: parameters are made on the GPU
+            col = ColumnParallelLinear(k, n, bias=True, params_dtype=torch.float16,
+                                       prefix="model.layers.0.self_attn.qkv_proj")
+            row = RowParallelLinear(n, k, bias=False, params_dtype=torch.float16,
+                                    prefix="model.layers.0.self_attn.o_proj")
+        assert col.weight.is_cuda and row.weight.is_cuda
         lo, hi = shard_range(n, rank, world)
         assert tuple(col.weight.shape) == (hi - lo, k) and tuple(row.weight.shape) == (k, hi - lo)
         with torch.no_grad():
