@@ -401,13 +401,23 @@ def run_gpu(args) -> int:
     # At TP > 1 the step is replayed from a CUDA graph: its ~20 launches are
     # host-bound otherwise (the GEMMs of a TP8 step last tens of microseconds).
     use_graph = args.graph == "on" or (args.graph == "auto" and world > 1)
+    lpg = min(max(1, args.layers_per_graph), args.steps) if use_graph and streams is not None and not sp else 1
+    args.lpg_used = lpg
     graphs, launches_per_step = [], None
     if use_graph:
         # the sequence-parallel step must not reuse an output buffer on
         # consecutive steps (other ranks read it), so it is captured twice.
         # The list is the only owner of the graphs (they may hold NCCL calls):
         # clearing it before destroy_process_group frees them all.
-        graphs, launches_per_step = capture_steps(lambda: step(x), 2 if sp else 1)
+        if lpg > 1:
+            # lpg consecutive layer steps per graph (lanes joined at its ends)
+            # plus a one-step graph for the remainder of --steps
+            graphs, per = capture_steps(lambda: layer.forward_overlapped_layers(x, streams, lpg), 1)
+            launches_per_step = per // lpg
+            tail, _ = capture_steps(lambda: step(x), 1)
+            graphs += tail
+        else:
+            graphs, launches_per_step = capture_steps(lambda: step(x), 2 if sp else 1)
         for i in range(4):
             graphs[i % len(graphs)].replay()
         barrier()
@@ -419,11 +429,17 @@ def run_gpu(args) -> int:
     with ClockSampler(local) as clocks:
         barrier()
         start.record()
-        for i in range(args.steps):
-            if graphs:
-                graphs[i % len(graphs)].replay()
-            else:
-                step(x, {"gate_up": ev[i]})
+        if lpg > 1:
+            for _ in range(args.steps // lpg):
+                graphs[0].replay()
+            for _ in range(args.steps % lpg):
+                graphs[1].replay()
+        else:
+            for i in range(args.steps):
+                if graphs:
+                    graphs[i % len(graphs)].replay()
+                else:
+                    step(x, {"gate_up": ev[i]})
         end.record()
         torch.cuda.synchronize()
     check_device_error()  # a bounded wait that gave up invalidates the timed steps
@@ -477,7 +493,7 @@ def run_gpu(args) -> int:
                "l2": "inputs larger than L2 every step (436 MB of weights per layer at TP1), no flush",
                "allreduce": {"nvls": "zcutlass_nvls_allreduce (multimem.ld_reduce acc::f32 + multimem.st)",
                              "nccl": f"NCCL all_reduce, {args.chunks} row chunks", "none": "none (TP1)"}[comm],
-               "micro_batches": micro, "cuda_graph": use_graph,
+               "micro_batches": micro, "cuda_graph": use_graph, "layer_steps_per_graph": lpg,
                "sequence_parallel": sp, **({"sp_gather": args.sp_gather} if sp else {}),
                "order": "qkv -> o_proj (+all-reduce) -> gate_up -> down (+all-reduce)"}
         line = {
@@ -713,6 +729,10 @@ def main(argv=None) -> int:
                     help="independent row blocks per step, each on its own stream (0: 2 when TP > 1, else 1)")
     ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",
                     help="replay each step from a CUDA graph (auto: when TP > 1)")
+    ap.add_argument("--layers-per-graph", type=int, default=1,
+                    help="at TP > 1 with row blocks: consecutive layer steps captured in one CUDA graph, the "
+                         "blocks joined only at its ends (as a stack of layers runs), so one block's next layer "
+                         "overlaps another block's last all-reduce; every step does the full layer's work")
     ap.add_argument("--sp", type=int, default=0,
                     help="1: sequence-parallel layer (reduce-scatters, all-gathers fused into the GEMMs; NVLS only)")
     ap.add_argument("--sp-gather", choices=["copy", "fused"], default="copy",

@@ -145,8 +145,20 @@ def check_layer_overlap(tp: TPGroup, dev, use_nvls: bool) -> dict:
     # NVLS: same kernels, same per-element reduction -> bit-identical. NCCL may
     # pick another algorithm inside a graph, so only the tolerance applies there.
     assert graph_exact if use_nvls else graph_rel < 1e-3, f"graph replay differs ({'nvls' if use_nvls else 'nccl'})"
+    # several layer steps in one graph, the blocks joined only at its ends (bench --layers-per-graph)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+        ys = layer.forward_overlapped_layers(x, streams, 3)
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    layered = torch.cat([y.clone() for y in ys])
+    del graph
+    layered_rel = float((layered.float() - ov.float()).norm() / ov.float().norm())
+    assert bool((layered == ov).all()) if use_nvls else layered_rel < 1e-3, "layered graph differs"
     assert _native.device_error(True) == 0
-    return {"exact_fraction": exact, "rel_frobenius": rel, "graph_replays_exact": graph_exact}
+    return {"exact_fraction": exact, "rel_frobenius": rel, "graph_replays_exact": graph_exact,
+            "layered_rel_frobenius": layered_rel}
 
 
 def check_sequence_parallel(tp: TPGroup, dev) -> dict:

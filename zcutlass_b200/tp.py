@@ -620,3 +620,31 @@ class TPDecoderLinears:
         for s in streams:
             cur.wait_stream(s)
         return [c[2]["y"] for c in chains]
+
+    def forward_overlapped_layers(self, x, streams, layers: int, outs=None):
+        """`layers` consecutive layer steps over len(streams) independent row
+        blocks, as a stack of decoder layers runs them: each block's chain of
+        layers on its own stream and NVLS lane, the blocks joined only at the
+        end, so block j's next layer can start while block j + 1 is still in
+        the previous layer's all-reduce. Every layer step does the same work as
+        forward_overlapped (the input of each layer is x: the linears stand in
+        for whole layers). Returns the last layer's per-block outputs."""
+        import torch
+
+        n = len(streams)
+        cur = torch.cuda.current_stream(x.device)
+        for s in streams:
+            s.wait_stream(cur)
+        chains = []
+        for _ in range(layers):
+            chains = []
+            for j in range(n):
+                r0, r1 = shard_range(x.shape[0], j, n)
+                chains.append(self._steps(x[r0:r1], j, None if outs is None else outs[j], None))
+            for phase in (0, 1):
+                for j, s in enumerate(streams):
+                    with torch.cuda.stream(s):
+                        chains[j][phase]()
+        for s in streams:
+            cur.wait_stream(s)
+        return [c[2]["y"] for c in chains]
