@@ -103,7 +103,7 @@ def sel(m, n, k, dtype=N.BF16, **kw):
 
 
 def test_registered_operation_count():
-    assert N.lib().zcutlass_registered_gemm_operation_count() == 28
+    assert N.lib().zcutlass_registered_gemm_operation_count() == 30
 
 
 def test_shape_families_follow_reference_rules():

@@ -61,6 +61,7 @@ FAMILIES = {
     "pair256": "_256x256x64_2cta_persistent",
     "persistent256": "_128x256x64_ws_persistent",
     "persistent128": "_128x128x64_ws_persistent",
+    "persistent64": "_128x64x64_ws_persistent",
     "swapab16": "_16x128x64_swapab_splitk",
     "swapab32": "_32x128x64_swapab_splitk",
     "swapab64": "_64x128x64_swapab_splitk",
@@ -80,6 +81,7 @@ FAMILY_SHAPES = {
     "pair256": [(256, 256, 64), (300, 520, 200), (1000, 777, 1032), (2048, 4096, 1024), (4096, 1536, 8960)],
     "persistent256": [(128, 256, 64), (300, 520, 200), (1000, 777, 1032), (2048, 4096, 1024)],
     "persistent128": [(128, 128, 64), (129, 136, 72), (513, 1000, 520), (1536, 2048, 1536)],
+    "persistent64": [(128, 64, 64), (129, 72, 72), (513, 1000, 520), (256, 4096, 4096)],
     "swapab16": [(1, 128, 128), (7, 300, 200), (16, 1000, 4096), (13, 4096, 1032)],
     "swapab32": [(17, 128, 128), (32, 520, 777), (25, 2048, 2048)],
     "swapab64": [(33, 256, 256), (64, 1000, 1000), (48, 4096, 1536)],

@@ -206,7 +206,9 @@ class Sm100Operation final : public GemmOperation {
                         : desc_.tile_n == 256 ? PC::SplitK128x256
                                               : PC::SplitK128x128);
       default:
-        return want == (desc_.tile_n == 256 ? PC::Cta128x256 : PC::Cta128x128);
+        return want == (desc_.tile_n == 256   ? PC::Cta128x256
+                        : desc_.tile_n == 128 ? PC::Cta128x128
+                                              : PC::Cta128x64);
     }
   }
 
@@ -332,6 +334,8 @@ void register_builtin_operations() {
       {"zcutlass_sm100_tcgen05_f16_128x256x64_ws_persistent", DType::F16, K::UmmaPersistent, 128, 256, 64, 4, F::Large, E::TmemRegisterTma},
       {"zcutlass_sm100_tcgen05_bf16_128x128x64_ws_persistent", DType::BF16, K::UmmaPersistent, 128, 128, 64, 6, F::Prefill, E::TmemRegisterTma},
       {"zcutlass_sm100_tcgen05_f16_128x128x64_ws_persistent", DType::F16, K::UmmaPersistent, 128, 128, 64, 6, F::Prefill, E::TmemRegisterTma},
+      {"zcutlass_sm100_tcgen05_bf16_128x64x64_ws_persistent", DType::BF16, K::UmmaPersistent, 128, 64, 64, 8, F::Prefill, E::TmemRegisterTma},
+      {"zcutlass_sm100_tcgen05_f16_128x64x64_ws_persistent", DType::F16, K::UmmaPersistent, 128, 64, 64, 8, F::Prefill, E::TmemRegisterTma},
       {"zcutlass_sm100_tcgen05_bf16_repack_generic", DType::BF16, K::Repack, 128, 128, 64, 4, F::Fallback, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_f16_repack_generic", DType::F16, K::Repack, 128, 128, 64, 4, F::Fallback, E::RegisterLinear},
       {"zcutlass_sm100_mma_bf16_128x128x32_generic", DType::BF16, K::Generic, 128, 128, 32, 2, F::Fallback, E::RegisterLinear},

@@ -519,6 +519,8 @@ enum : int {
   kCfgSplitKF16N128,
   kCfgSplitKBf16M256,
   kCfgSplitKF16M256,
+  kCfgUmmaBf16N64,
+  kCfgUmmaF16N64,
   kCfgColMajorB = 32,
 };
 
@@ -543,6 +545,10 @@ cudaError_t launch_umma_km(const LaunchArgs& a, DeviceSlot* slot, int bn) {
   if (bn == 256) {
     return a.bf16 ? launch_umma_t<__nv_bfloat16, 256, 4, KM>(a, slot, kCfgUmmaBf16N256 + off)
                   : launch_umma_t<half, 256, 4, KM>(a, slot, kCfgUmmaF16N256 + off);
+  }
+  if (bn == 64) {
+    return a.bf16 ? launch_umma_t<__nv_bfloat16, 64, 8, KM>(a, slot, kCfgUmmaBf16N64 + off)
+                  : launch_umma_t<half, 64, 8, KM>(a, slot, kCfgUmmaF16N64 + off);
   }
   return a.bf16 ? launch_umma_t<__nv_bfloat16, 128, 6, KM>(a, slot, kCfgUmmaBf16N128 + off)
                 : launch_umma_t<half, 128, 6, KM>(a, slot, kCfgUmmaF16N128 + off);
@@ -592,7 +598,8 @@ TileChoice choose_tiles(int64_t m, int64_t n, int64_t k, int sm_count) {
   // 256 x 1536^2, 256 x 2048 x 1536, 256 x 14336 x 4096, 1024^3 and
   // 8192 x 28672 x 4096:
   //   persistent: waves x K blocks x clocks per K block of one tile + fixed
-  //     (CTA pair 256x256: 800 + 5000, 128x256: 820 + 7000, 128x128: 600 + 9000);
+  //     (CTA pair 256x256: 800 + 5000, 128x256: 820 + 7000, 128x128: 600 + 9000,
+  //     128x64: 610 + 6350);
   //   split-K (one wave): ceil(K blocks / S) x clocks per K block + fixed,
   //     the fixed part being mostly the cross-CTA reduction of the FP32
   //     partial through distributed shared memory (128x128: 645 + 12600,
@@ -611,6 +618,7 @@ TileChoice choose_tiles(int64_t m, int64_t n, int64_t k, int sm_count) {
       {PersistentConfig::Pair256x256, 256, 256, pairs, 800.0, 5000.0, false},
       {PersistentConfig::Cta128x256, 128, 256, sm_count, 820.0, 7000.0, false},
       {PersistentConfig::Cta128x128, 128, 128, sm_count, 600.0, 9000.0, false},
+      {PersistentConfig::Cta128x64, 128, 64, sm_count, 610.0, 6350.0, false},
       {PersistentConfig::SplitK256x256, 256, 256, sm_count, 1450.0, 40000.0, true},
       {PersistentConfig::SplitK128x256, 128, 256, sm_count, 990.0, 15500.0, true},
       {PersistentConfig::SplitK128x128, 128, 128, sm_count, 645.0, 12600.0, true},
@@ -694,7 +702,7 @@ cudaError_t launch_umma_gemm(const LaunchArgs& a, int bn) {
   DeviceSlot* slot = current_slot();
   if (slot == nullptr) return cudaErrorInvalidDevice;
   if (a.a_nparts > 1) {
-    if (!a.b_col_major || a.a_nparts > kMaxAParts) return cudaErrorInvalidValue;
+    if (!a.b_col_major || a.a_nparts > kMaxAParts || bn == 64) return cudaErrorInvalidValue;
     if (bn == 256) {
       return a.bf16 ? launch_umma_t<__nv_bfloat16, 256, 4, true, kMaxAParts>(a, slot, kCfgGatherUmmaBf16N256)
                     : launch_umma_t<half, 256, 4, true, kMaxAParts>(a, slot, kCfgGatherUmmaF16N256);
@@ -918,6 +926,9 @@ cudaError_t launch_repack_gemm(const LaunchArgs& a) {
         break;
       case PersistentConfig::Cta128x128:
         e = launch_umma_gemm(b, 128);
+        break;
+      case PersistentConfig::Cta128x64:
+        e = launch_umma_gemm(b, 64);
         break;
       case PersistentConfig::SplitK256x256:
         e = launch_umma_splitk_gemm(b, 256, 256, tc.splits);

@@ -77,7 +77,7 @@ bool repack_ready_for_stream(size_t bytes, cudaStream_t stream);
 cudaError_t launch_umma_splitk_gemm(const LaunchArgs& args, int bm, int bn, int splits);
 
 // Shape heuristics shared by dispatch and telemetry.
-enum class PersistentConfig { Pair256x256, Cta128x256, Cta128x128, SplitK256x256, SplitK128x256, SplitK128x128 };
+enum class PersistentConfig { Pair256x256, Cta128x256, Cta128x128, SplitK256x256, SplitK128x256, SplitK128x128, Cta128x64 };
 // The persistent configurations only (no split-K): for paths whose kernels
 // need one CTA (pair) per output tile.
 PersistentConfig choose_persistent(int64_t m, int64_t n, int sm_count);
