@@ -332,10 +332,10 @@ void register_builtin_operations() {
       {"zcutlass_sm100_tcgen05_f16_256x256x64_2cta_persistent", DType::F16, K::UmmaPair, 256, 256, 64, 6, F::Large, E::TmemRegisterTma},
       {"zcutlass_sm100_tcgen05_bf16_128x256x64_ws_persistent", DType::BF16, K::UmmaPersistent, 128, 256, 64, 4, F::Large, E::TmemRegisterTma},
       {"zcutlass_sm100_tcgen05_f16_128x256x64_ws_persistent", DType::F16, K::UmmaPersistent, 128, 256, 64, 4, F::Large, E::TmemRegisterTma},
-      {"zcutlass_sm100_tcgen05_bf16_128x128x64_ws_persistent", DType::BF16, K::UmmaPersistent, 128, 128, 64, 6, F::Prefill, E::TmemRegisterTma},
-      {"zcutlass_sm100_tcgen05_f16_128x128x64_ws_persistent", DType::F16, K::UmmaPersistent, 128, 128, 64, 6, F::Prefill, E::TmemRegisterTma},
-      {"zcutlass_sm100_tcgen05_bf16_128x64x64_ws_persistent", DType::BF16, K::UmmaPersistent, 128, 64, 64, 8, F::Prefill, E::TmemRegisterTma},
-      {"zcutlass_sm100_tcgen05_f16_128x64x64_ws_persistent", DType::F16, K::UmmaPersistent, 128, 64, 64, 8, F::Prefill, E::TmemRegisterTma},
+      {"zcutlass_sm100_tcgen05_bf16_128x128x64_ws_persistent", DType::BF16, K::UmmaPersistent, 128, 128, 64, 3, F::Prefill, E::TmemRegisterTma},
+      {"zcutlass_sm100_tcgen05_f16_128x128x64_ws_persistent", DType::F16, K::UmmaPersistent, 128, 128, 64, 3, F::Prefill, E::TmemRegisterTma},
+      {"zcutlass_sm100_tcgen05_bf16_128x64x64_ws_persistent", DType::BF16, K::UmmaPersistent, 128, 64, 64, 4, F::Prefill, E::TmemRegisterTma},
+      {"zcutlass_sm100_tcgen05_f16_128x64x64_ws_persistent", DType::F16, K::UmmaPersistent, 128, 64, 64, 4, F::Prefill, E::TmemRegisterTma},
       {"zcutlass_sm100_tcgen05_bf16_repack_generic", DType::BF16, K::Repack, 128, 128, 64, 4, F::Fallback, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_f16_repack_generic", DType::F16, K::Repack, 128, 128, 64, 4, F::Fallback, E::RegisterLinear},
       {"zcutlass_sm100_mma_bf16_128x128x32_generic", DType::BF16, K::Generic, 128, 128, 32, 2, F::Fallback, E::RegisterLinear},

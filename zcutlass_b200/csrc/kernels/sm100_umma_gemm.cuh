@@ -58,11 +58,16 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
   return (2 * bn) <= 32 ? 32 : (2 * bn) <= 64 ? 64 : (2 * bn) <= 128 ? 128 : (2 * bn) <= 256 ? 256 : 512;
 }
 
-template <int BN, int STAGES>
+// A stage holds KSUB sub-blocks of 64 K: one TMA unit streams faster with
+// larger stages at the same bytes in flight (mid-size problems, where few
+// tiles per SM leave each SM's load rate as the limit).
+template <int BN, int STAGES, int KSUB = 1>
 struct Smem {
-  static constexpr int kABytes = kBlockM * kBlockK * 2;        // 16 KiB
+  static constexpr int kASubBytes = kBlockM * kBlockK * 2;     // 16 KiB
   static constexpr int kBChunkBytes = kBlockK * 128;           // one 64(N) x 64(K) box: 8 KiB
-  static constexpr int kBBytes = (BN / 64) * kBChunkBytes;     // BN=256: 32 KiB
+  static constexpr int kBSubBytes = (BN / 64) * kBChunkBytes;  // BN=256: 32 KiB
+  static constexpr int kABytes = KSUB * kASubBytes;
+  static constexpr int kBBytes = KSUB * kBSubBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiBufBytes = 32 * kEpiCols * 2;       // 2 KiB
   static constexpr int kAOff = 0;
@@ -127,11 +132,11 @@ __device__ __forceinline__ void store_row_prefix(T* dst, const uint32_t (&packed
 
 // kBKMajor: B is given column-major (B[k][n] at n*ldb + k, i.e. a PyTorch
 // [N, K] weight); its tiles are then K-major like A's.
-template <typename T, int BN, int STAGES, bool kBKMajor, int kAParts = 1>
+template <typename T, int BN, int STAGES, bool kBKMajor, int kAParts = 1, int KSUB = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ TmaMapSet<kAParts> amaps, const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_d, const UmmaGemmParams p) {
-  using L = Smem<BN, STAGES>;
+  using L = Smem<BN, STAGES, KSUB>;
   constexpr uint32_t kTmemCols = tmem_cols_for(BN);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -194,14 +199,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[s], L::kStageBytes);
-          tma_load_2d(smem + L::kAOff + s * L::kABytes, tmap_a, &full[s], kb * kBlockK, m0);
-          if constexpr (kBKMajor) {
-            tma_load_2d(smem + L::kBOff + s * L::kBBytes, &tmap_b, &full[s], kb * kBlockK, n0);
-          } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) {
-              tma_load_2d(smem + L::kBOff + s * L::kBBytes + j * L::kBChunkBytes, &tmap_b,
-                          &full[s], n0 + 64 * j, kb * kBlockK);
+          for (int sub = 0; sub < KSUB; ++sub) {
+            const int k0 = (kb * KSUB + sub) * kBlockK;
+            uint8_t* a_dst = smem + L::kAOff + s * L::kABytes + sub * L::kASubBytes;
+            uint8_t* b_dst = smem + L::kBOff + s * L::kBBytes + sub * L::kBSubBytes;
+            tma_load_2d(a_dst, tmap_a, &full[s], k0, m0);
+            if constexpr (kBKMajor) {
+              tma_load_2d(b_dst, &tmap_b, &full[s], k0, n0);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j)
+                tma_load_2d(b_dst + j * L::kBChunkBytes, &tmap_b, &full[s], n0 + 64 * j, k0);
             }
           }
         }
@@ -236,19 +245,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after_sync();
-          const uint32_t a_addr = smem_addr(smem + L::kAOff + s * L::kABytes);
-          const uint32_t b_addr = smem_addr(smem + L::kBOff + s * L::kBBytes);
 #pragma unroll
-          for (int kk = 0; kk < kBlockK / kUmmaK; ++kk) {
-            // A: K-major rows of 128 B; a 16-wide K slice starts 32 B further in.
-            const uint64_t a_desc = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
-            // B N-major: 64-column atoms are kBChunkBytes apart (LBO), 8-row
-            // K groups 1024 B apart (SBO); a K slice of 16 rows is 2048 B.
-            // B K-major: same form as A.
-            const uint64_t b_desc = kBKMajor
-                                        ? smem_desc_sw128(b_addr + kk * 32, 16, 1024)
-                                        : smem_desc_sw128(b_addr + kk * 2048, L::kBChunkBytes, 1024);
-            umma_f16_ss(d_tmem, a_desc, b_desc, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+          for (int sub = 0; sub < KSUB; ++sub) {
+            const uint32_t a_addr = smem_addr(smem + L::kAOff + s * L::kABytes + sub * L::kASubBytes);
+            const uint32_t b_addr = smem_addr(smem + L::kBOff + s * L::kBBytes + sub * L::kBSubBytes);
+#pragma unroll
+            for (int kk = 0; kk < kBlockK / kUmmaK; ++kk) {
+              // A: K-major rows of 128 B; a 16-wide K slice starts 32 B further in.
+              const uint64_t a_desc = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+              // B N-major: 64-column atoms are kBChunkBytes apart (LBO), 8-row
+              // K groups 1024 B apart (SBO); a K slice of 16 rows is 2048 B.
+              // B K-major: same form as A.
+              const uint64_t b_desc = kBKMajor
+                                          ? smem_desc_sw128(b_addr + kk * 32, 16, 1024)
+                                          : smem_desc_sw128(b_addr + kk * 2048, L::kBChunkBytes, 1024);
+              umma_f16_ss(d_tmem, a_desc, b_desc, kIdesc, (kb | sub | kk) != 0 ? 1u : 0u);
+            }
           }
           issued = true;
           umma_commit(&empty[s]);

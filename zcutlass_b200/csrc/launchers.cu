@@ -109,9 +109,9 @@ bool make_a_maps(TmaMapSet<AP>* set, const LaunchArgs& a, int box_rows, int box_
   return true;
 }
 
-template <typename T, int BN, int STAGES, bool KM, int AP = 1>
+template <typename T, int BN, int STAGES, bool KM, int AP = 1, int KSUB = 1>
 cudaError_t launch_umma_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit) {
-  using L = umma::Smem<BN, STAGES>;
+  using L = umma::Smem<BN, STAGES, KSUB>;
   TmaMapSet<AP> ta;
   CUtensorMap tb, td;
   const bool bf16 = a.bf16;
@@ -127,7 +127,7 @@ cudaError_t launch_umma_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit)
   p.k = static_cast<int>(a.k);
   p.tiles_m = static_cast<int>((a.m + umma::kBlockM - 1) / umma::kBlockM);
   p.tiles_n = static_cast<int>((a.n + BN - 1) / BN);
-  p.num_kb = static_cast<int>((a.k + umma::kBlockK - 1) / umma::kBlockK);
+  p.num_kb = static_cast<int>((a.k + KSUB * umma::kBlockK - 1) / (KSUB * umma::kBlockK));
   p.total_tiles = p.tiles_m * p.tiles_n;
   p.group_m = std::min(p.tiles_m, 16);
   p.alpha = a.alpha;
@@ -142,7 +142,7 @@ cudaError_t launch_umma_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit)
   p.a_rows_per_part = AP == 1 ? 0 : static_cast<int>(a.a_rows_per_part);
   p.a_parts = AP == 1 ? 1 : a.a_nparts;
 
-  auto kernel = umma::gemm_kernel<T, BN, STAGES, KM, AP>;
+  auto kernel = umma::gemm_kernel<T, BN, STAGES, KM, AP, KSUB>;
   cudaError_t e = ensure_smem_attr(slot, config_bit, kernel, L::kDynamicBytes);
   if (e != cudaSuccess) return e;
   const int grid = std::min(p.total_tiles, slot->info.sm_count);
@@ -547,11 +547,11 @@ cudaError_t launch_umma_km(const LaunchArgs& a, DeviceSlot* slot, int bn) {
                   : launch_umma_t<half, 256, 4, KM>(a, slot, kCfgUmmaF16N256 + off);
   }
   if (bn == 64) {
-    return a.bf16 ? launch_umma_t<__nv_bfloat16, 64, 8, KM>(a, slot, kCfgUmmaBf16N64 + off)
-                  : launch_umma_t<half, 64, 8, KM>(a, slot, kCfgUmmaF16N64 + off);
+    return a.bf16 ? launch_umma_t<__nv_bfloat16, 64, 4, KM, 1, 2>(a, slot, kCfgUmmaBf16N64 + off)
+                  : launch_umma_t<half, 64, 4, KM, 1, 2>(a, slot, kCfgUmmaF16N64 + off);
   }
-  return a.bf16 ? launch_umma_t<__nv_bfloat16, 128, 6, KM>(a, slot, kCfgUmmaBf16N128 + off)
-                : launch_umma_t<half, 128, 6, KM>(a, slot, kCfgUmmaF16N128 + off);
+  return a.bf16 ? launch_umma_t<__nv_bfloat16, 128, 3, KM, 1, 2>(a, slot, kCfgUmmaBf16N128 + off)
+                : launch_umma_t<half, 128, 3, KM, 1, 2>(a, slot, kCfgUmmaF16N128 + off);
 }
 
 template <bool KM>
@@ -598,8 +598,8 @@ TileChoice choose_tiles(int64_t m, int64_t n, int64_t k, int sm_count) {
   // 256 x 1536^2, 256 x 2048 x 1536, 256 x 14336 x 4096, 1024^3 and
   // 8192 x 28672 x 4096:
   //   persistent: waves x K blocks x clocks per K block of one tile + fixed
-  //     (CTA pair 256x256: 800 + 5000, 128x256: 820 + 7000, 128x128: 600 + 9000,
-  //     128x64: 610 + 6350);
+  //     (CTA pair 256x256: 800 + 5000, 128x256: 820 + 7000, 128x128: 560 + 5000,
+  //     128x64: 454 + 6290; the last two stream two 64-wide K blocks per stage);
   //   split-K (one wave): ceil(K blocks / S) x clocks per K block + fixed,
   //     the fixed part being mostly the cross-CTA reduction of the FP32
   //     partial through distributed shared memory (128x128: 645 + 12600,
@@ -617,8 +617,8 @@ TileChoice choose_tiles(int64_t m, int64_t n, int64_t k, int sm_count) {
   const Cand cands[] = {
       {PersistentConfig::Pair256x256, 256, 256, pairs, 800.0, 5000.0, false},
       {PersistentConfig::Cta128x256, 128, 256, sm_count, 820.0, 7000.0, false},
-      {PersistentConfig::Cta128x128, 128, 128, sm_count, 600.0, 9000.0, false},
-      {PersistentConfig::Cta128x64, 128, 64, sm_count, 610.0, 6350.0, false},
+      {PersistentConfig::Cta128x128, 128, 128, sm_count, 560.0, 5000.0, false},
+      {PersistentConfig::Cta128x64, 128, 64, sm_count, 454.0, 6290.0, false},
       {PersistentConfig::SplitK256x256, 256, 256, sm_count, 1450.0, 40000.0, true},
       {PersistentConfig::SplitK128x256, 128, 256, sm_count, 990.0, 15500.0, true},
       {PersistentConfig::SplitK128x128, 128, 128, sm_count, 645.0, 12600.0, true},
