@@ -125,7 +125,7 @@ def test_dispatch_table_on_b200():
     assert "f16_32x128x64_swapab" in sel(20, 4096, 4096, dtype=N.F16)["kernel_name"]
     assert "64x128x64_swapab" in sel(64, 1024, 1024)["kernel_name"]
     # mid-M: too few output tiles for 148 SMs -> cluster split-K
-    assert "128x256x64_splitk_cluster" in sel(256, 4096, 4096)["kernel_name"]
+    assert "128x128x64_splitk_cluster" in sel(256, 4096, 4096)["kernel_name"]
     assert "128x128x64_splitk_cluster" in sel(128, 4096, 4096)["kernel_name"]
     # one wave of 128 x 128 tiles with the two-block stages beats splitting K
     assert "128x128x64_ws_persistent" in sel(512, 4096, 4096)["kernel_name"]

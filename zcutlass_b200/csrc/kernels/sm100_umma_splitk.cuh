@@ -54,11 +54,15 @@ constexpr int kEpiWarps = 4;
 constexpr int kMaxSplits = 8;  // portable cluster size
 constexpr int kUnroll = 2;     // reduction groups per thread per pass
 
-template <int BM, int BN, int STAGES>
+// A stage holds KSUB sub-blocks of 64 K (larger stages stream faster per SM
+// at the same bytes in flight).
+template <int BM, int BN, int STAGES, int KSUB = 1>
 struct Smem {
-  static constexpr int kABytes = BM * kBlockK * 2;          // 16 or 32 KiB
+  static constexpr int kASubBytes = BM * kBlockK * 2;       // 16 or 32 KiB
   static constexpr int kBChunkBytes = kBlockK * 128;        // 64(n) x 64(k) box: 8 KiB
-  static constexpr int kBBytes = (BN / 64) * kBChunkBytes;
+  static constexpr int kBSubBytes = (BN / 64) * kBChunkBytes;
+  static constexpr int kABytes = KSUB * kASubBytes;
+  static constexpr int kBBytes = KSUB * kBSubBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kAOff = 0;
   static constexpr int kBOff = STAGES * kABytes;
@@ -140,11 +144,11 @@ __device__ __forceinline__ void store_group(T* dptr, const T* cptr, const T* bpt
 }
 
 // kBKMajor: B is column-major (a PyTorch [N, K] weight): its tiles are K-major.
-template <typename T, int BM, int BN, int STAGES, bool kBKMajor>
+template <typename T, int BM, int BN, int STAGES, bool kBKMajor, int KSUB = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                 const SplitKParams p) {
-  using L = Smem<BM, BN, STAGES>;
+  using L = Smem<BM, BN, STAGES, KSUB>;
   constexpr int kHalves = BM / kBlockM;
   constexpr uint32_t kTmemCols = kHalves * BN;  // accumulator h at columns [h*BN, (h+1)*BN)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -204,14 +208,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         mbar_arrive_expect_tx(&full[s], L::kStageBytes);
-        tma_load_2d(smem + L::kAOff + s * L::kABytes, &tmap_a, &full[s], kb * kBlockK, m0);
-        if constexpr (kBKMajor) {
-          tma_load_2d(smem + L::kBOff + s * L::kBBytes, &tmap_b, &full[s], kb * kBlockK, n0);
-        } else {
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j)
-            tma_load_2d(smem + L::kBOff + s * L::kBBytes + j * L::kBChunkBytes, &tmap_b, &full[s], n0 + 64 * j,
-                        kb * kBlockK);
+        for (int sub = 0; sub < KSUB; ++sub) {
+          const int k0 = (kb * KSUB + sub) * kBlockK;
+          uint8_t* b_dst = smem + L::kBOff + s * L::kBBytes + sub * L::kBSubBytes;
+          tma_load_2d(smem + L::kAOff + s * L::kABytes + sub * L::kASubBytes, &tmap_a, &full[s], k0, m0);
+          if constexpr (kBKMajor) {
+            tma_load_2d(b_dst, &tmap_b, &full[s], k0, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(b_dst + j * L::kBChunkBytes, &tmap_b, &full[s], n0 + 64 * j, k0);
+          }
         }
       }
       if (!ok) {
@@ -232,16 +240,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after_sync();
-        const uint32_t a_addr = smem_addr(smem + L::kAOff + s * L::kABytes);
-        const uint32_t b_addr = smem_addr(smem + L::kBOff + s * L::kBBytes);
 #pragma unroll
-        for (int kk = 0; kk < kBlockK / kUmmaK; ++kk) {
-          const uint64_t b_desc = kBKMajor ? smem_desc_sw128(b_addr + kk * 32, 16, 1024)
-                                           : smem_desc_sw128(b_addr + kk * 2048, L::kBChunkBytes, 1024);
+        for (int sub = 0; sub < KSUB; ++sub) {
+          const uint32_t a_addr = smem_addr(smem + L::kAOff + s * L::kABytes + sub * L::kASubBytes);
+          const uint32_t b_addr = smem_addr(smem + L::kBOff + s * L::kBBytes + sub * L::kBSubBytes);
 #pragma unroll
-          for (int h = 0; h < kHalves; ++h) {  // rows [128h, 128h + 128) of the A tile: 16 KiB apart
-            const uint64_t a_desc = smem_desc_sw128(a_addr + h * 16384 + kk * 32, 16, 1024);
-            umma_f16_ss(tmem_base + h * BN, a_desc, b_desc, kIdesc, (it | kk) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < kBlockK / kUmmaK; ++kk) {
+            const uint64_t b_desc = kBKMajor ? smem_desc_sw128(b_addr + kk * 32, 16, 1024)
+                                             : smem_desc_sw128(b_addr + kk * 2048, L::kBChunkBytes, 1024);
+#pragma unroll
+            for (int h = 0; h < kHalves; ++h) {  // rows [128h, 128h + 128) of the A tile: 16 KiB apart
+              const uint64_t a_desc = smem_desc_sw128(a_addr + h * 16384 + kk * 32, 16, 1024);
+              umma_f16_ss(tmem_base + h * BN, a_desc, b_desc, kIdesc, (it | sub | kk) != 0 ? 1u : 0u);
+            }
           }
         }
         issued = true;

@@ -286,9 +286,9 @@ cudaError_t launch_umma2_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit
   return cudaGetLastError();
 }
 
-template <typename T, int BM, int BN, int STAGES, bool KM>
+template <typename T, int BM, int BN, int STAGES, bool KM, int KSUB = 1>
 cudaError_t launch_splitk_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit, int splits) {
-  using L = splitk::Smem<BM, BN, STAGES>;
+  using L = splitk::Smem<BM, BN, STAGES, KSUB>;
   CUtensorMap ta, tb;
   const bool bf16 = a.bf16;
   const bool b_ok = KM ? make_tma_2d(&tb, a.b, bf16, a.n, a.k, a.ldb, BN, splitk::kBlockK, TmaSwizzle::B128)
@@ -302,7 +302,7 @@ cudaError_t launch_splitk_t(const LaunchArgs& a, DeviceSlot* slot, int config_bi
   p.m = static_cast<int>(a.m);
   p.n = static_cast<int>(a.n);
   p.k = static_cast<int>(a.k);
-  p.num_kb = static_cast<int>((a.k + splitk::kBlockK - 1) / splitk::kBlockK);
+  p.num_kb = static_cast<int>((a.k + KSUB * splitk::kBlockK - 1) / (KSUB * splitk::kBlockK));
   p.alpha = a.alpha;
   p.beta = a.beta;
   p.c = a.c;
@@ -313,7 +313,7 @@ cudaError_t launch_splitk_t(const LaunchArgs& a, DeviceSlot* slot, int config_bi
   p.epi_flags = (a.beta != 0.0f ? kEpiHasC : 0u) | (a.bias != nullptr ? kEpiHasBias : 0u);
   p.error_word = slot->info.error_word;
 
-  auto kernel = splitk::gemm_kernel<T, BM, BN, STAGES, KM>;
+  auto kernel = splitk::gemm_kernel<T, BM, BN, STAGES, KM, KSUB>;
   cudaError_t e = ensure_smem_attr(slot, config_bit, kernel, L::kDynamicBytes);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg{};
@@ -565,8 +565,8 @@ cudaError_t launch_splitk_km(const LaunchArgs& a, DeviceSlot* slot, int bm, int 
     return a.bf16 ? launch_splitk_t<__nv_bfloat16, 128, 256, 4, KM>(a, slot, kCfgSplitKBf16N256 + off, splits)
                   : launch_splitk_t<half, 128, 256, 4, KM>(a, slot, kCfgSplitKF16N256 + off, splits);
   }
-  return a.bf16 ? launch_splitk_t<__nv_bfloat16, 128, 128, 6, KM>(a, slot, kCfgSplitKBf16N128 + off, splits)
-                : launch_splitk_t<half, 128, 128, 6, KM>(a, slot, kCfgSplitKF16N128 + off, splits);
+  return a.bf16 ? launch_splitk_t<__nv_bfloat16, 128, 128, 3, KM, 2>(a, slot, kCfgSplitKBf16N128 + off, splits)
+                : launch_splitk_t<half, 128, 128, 3, KM, 2>(a, slot, kCfgSplitKF16N128 + off, splits);
 }
 
 template <bool KM>
@@ -602,7 +602,8 @@ TileChoice choose_tiles(int64_t m, int64_t n, int64_t k, int sm_count) {
   //     128x64: 454 + 6290; the last two stream two 64-wide K blocks per stage);
   //   split-K (one wave): ceil(K blocks / S) x clocks per K block + fixed,
   //     the fixed part being mostly the cross-CTA reduction of the FP32
-  //     partial through distributed shared memory (128x128: 645 + 12600,
+  //     partial through distributed shared memory (128x128, two 64-wide K
+  //     blocks per stage: 560 + 12900,
   //     128x256: 990 + 15500, 256x256: 1450 + 40000).
   // It picks the fastest measured configuration on each of those shapes
   // (within 3 %).
@@ -621,7 +622,7 @@ TileChoice choose_tiles(int64_t m, int64_t n, int64_t k, int sm_count) {
       {PersistentConfig::Cta128x64, 128, 64, sm_count, 454.0, 6290.0, false},
       {PersistentConfig::SplitK256x256, 256, 256, sm_count, 1450.0, 40000.0, true},
       {PersistentConfig::SplitK128x256, 128, 256, sm_count, 990.0, 15500.0, true},
-      {PersistentConfig::SplitK128x128, 128, 128, sm_count, 645.0, 12600.0, true},
+      {PersistentConfig::SplitK128x128, 128, 128, sm_count, 560.0, 12900.0, true},
   };
   const char* forced = std::getenv("ZCUTLASS_SPLITK");
   const int forced_splits = forced != nullptr ? std::atoi(forced) : 0;
