@@ -120,7 +120,7 @@ def test_dispatch_table_on_b200():
     big = sel(8192, 28672, 4096)
     assert "256x256x64_2cta_persistent" in big["kernel_name"]
     assert big["kernel_path"] == "fast" and big["epilogue_kind"] == "tmem_register_tma"
-    assert big["tile"] == {"m": 256, "n": 256, "k": 64} and big["pipeline_stages"] == 6
+    assert big["tile"] == {"m": 256, "n": 256, "k": 64} and big["pipeline_stages"] == 3
     assert "bf16_16x128x64_swapab" in sel(8, 4096, 4096)["kernel_name"]
     assert "f16_32x128x64_swapab" in sel(20, 4096, 4096, dtype=N.F16)["kernel_name"]
     assert "64x128x64_swapab" in sel(64, 1024, 1024)["kernel_name"]

@@ -328,8 +328,8 @@ void register_builtin_operations() {
       {"zcutlass_sm100_tcgen05_f16_128x256x64_splitk_cluster", DType::F16, K::UmmaSplitK, 128, 256, 64, 4, F::Prefill, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_bf16_128x128x64_splitk_cluster", DType::BF16, K::UmmaSplitK, 128, 128, 64, 3, F::Prefill, E::RegisterLinear},
       {"zcutlass_sm100_tcgen05_f16_128x128x64_splitk_cluster", DType::F16, K::UmmaSplitK, 128, 128, 64, 3, F::Prefill, E::RegisterLinear},
-      {"zcutlass_sm100_tcgen05_bf16_256x256x64_2cta_persistent", DType::BF16, K::UmmaPair, 256, 256, 64, 6, F::Large, E::TmemRegisterTma},
-      {"zcutlass_sm100_tcgen05_f16_256x256x64_2cta_persistent", DType::F16, K::UmmaPair, 256, 256, 64, 6, F::Large, E::TmemRegisterTma},
+      {"zcutlass_sm100_tcgen05_bf16_256x256x64_2cta_persistent", DType::BF16, K::UmmaPair, 256, 256, 64, 3, F::Large, E::TmemRegisterTma},
+      {"zcutlass_sm100_tcgen05_f16_256x256x64_2cta_persistent", DType::F16, K::UmmaPair, 256, 256, 64, 3, F::Large, E::TmemRegisterTma},
       {"zcutlass_sm100_tcgen05_bf16_128x256x64_ws_persistent", DType::BF16, K::UmmaPersistent, 128, 256, 64, 4, F::Large, E::TmemRegisterTma},
       {"zcutlass_sm100_tcgen05_f16_128x256x64_ws_persistent", DType::F16, K::UmmaPersistent, 128, 256, 64, 4, F::Large, E::TmemRegisterTma},
       {"zcutlass_sm100_tcgen05_bf16_128x128x64_ws_persistent", DType::BF16, K::UmmaPersistent, 128, 128, 64, 3, F::Prefill, E::TmemRegisterTma},

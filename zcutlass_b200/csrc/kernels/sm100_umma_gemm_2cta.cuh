@@ -36,11 +36,14 @@ constexpr int kEpiWarps = 4;
 constexpr int kEpiCols = 32;
 constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
 
-template <int STAGES>
+// A stage holds KSUB sub-blocks of 64 K per CTA.
+template <int STAGES, int KSUB = 1>
 struct Smem {
-  static constexpr int kABytes = kHalfM * kBlockK * 2;   // 16 KiB
-  static constexpr int kBChunkBytes = kBlockK * 128;     // 64(n) x 64(k) N-major box: 8 KiB
-  static constexpr int kBBytes = kHalfN * kBlockK * 2;   // 16 KiB
+  static constexpr int kASubBytes = kHalfM * kBlockK * 2;  // 16 KiB
+  static constexpr int kBChunkBytes = kBlockK * 128;       // 64(n) x 64(k) N-major box: 8 KiB
+  static constexpr int kBSubBytes = kHalfN * kBlockK * 2;  // 16 KiB
+  static constexpr int kABytes = KSUB * kASubBytes;
+  static constexpr int kBBytes = KSUB * kBSubBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;  // per CTA
   static constexpr int kEpiBufBytes = 32 * kEpiCols * 2;
   static constexpr int kAOff = 0;
@@ -61,11 +64,11 @@ enum : int {
   kErrEpiTmemFull = (11 << 4) | 3,
 };
 
-template <typename T, int STAGES, bool kBKMajor, int kAParts = 1>
+template <typename T, int STAGES, bool kBKMajor, int kAParts = 1, int KSUB = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ TmaMapSet<kAParts> amaps, const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_d, const UmmaGemmParams p) {
-  using L = Smem<STAGES>;
+  using L = Smem<STAGES, KSUB>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -133,13 +136,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint32_t full_leader = map_shared_rank(smem_addr(&full[s]), 0);
           if (leader) mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);
-          tma_load_2d_pair(smem + L::kAOff + s * L::kABytes, tmap_a, full_leader, kb * kBlockK, m0);
-          uint8_t* sb = smem + L::kBOff + s * L::kBBytes;
-          if constexpr (kBKMajor) {
-            tma_load_2d_pair(sb, &tmap_b, full_leader, kb * kBlockK, nb);
-          } else {
-            tma_load_2d_pair(sb, &tmap_b, full_leader, nb, kb * kBlockK);
-            tma_load_2d_pair(sb + L::kBChunkBytes, &tmap_b, full_leader, nb + 64, kb * kBlockK);
+#pragma unroll
+          for (int sub = 0; sub < KSUB; ++sub) {
+            const int k0 = (kb * KSUB + sub) * kBlockK;
+            tma_load_2d_pair(smem + L::kAOff + s * L::kABytes + sub * L::kASubBytes, tmap_a, full_leader, k0, m0);
+            uint8_t* sb = smem + L::kBOff + s * L::kBBytes + sub * L::kBSubBytes;
+            if constexpr (kBKMajor) {
+              tma_load_2d_pair(sb, &tmap_b, full_leader, k0, nb);
+            } else {
+              tma_load_2d_pair(sb, &tmap_b, full_leader, nb, k0);
+              tma_load_2d_pair(sb + L::kBChunkBytes, &tmap_b, full_leader, nb + 64, k0);
+            }
           }
         }
       }
@@ -177,14 +184,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after_sync();
-          const uint32_t a_addr = smem_addr(smem + L::kAOff + s * L::kABytes);
-          const uint32_t b_addr = smem_addr(smem + L::kBOff + s * L::kBBytes);
 #pragma unroll
-          for (int kk = 0; kk < kBlockK / 16; ++kk) {
-            const uint64_t a_desc = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
-            const uint64_t b_desc = kBKMajor ? smem_desc_sw128(b_addr + kk * 32, 16, 1024)
-                                             : smem_desc_sw128(b_addr + kk * 2048, L::kBChunkBytes, 1024);
-            umma_f16_ss_pair(d_tmem, a_desc, b_desc, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+          for (int sub = 0; sub < KSUB; ++sub) {
+            const uint32_t a_addr = smem_addr(smem + L::kAOff + s * L::kABytes + sub * L::kASubBytes);
+            const uint32_t b_addr = smem_addr(smem + L::kBOff + s * L::kBBytes + sub * L::kBSubBytes);
+#pragma unroll
+            for (int kk = 0; kk < kBlockK / 16; ++kk) {
+              const uint64_t a_desc = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+              const uint64_t b_desc = kBKMajor ? smem_desc_sw128(b_addr + kk * 32, 16, 1024)
+                                               : smem_desc_sw128(b_addr + kk * 2048, L::kBChunkBytes, 1024);
+              umma_f16_ss_pair(d_tmem, a_desc, b_desc, kIdesc, (kb | sub | kk) != 0 ? 1u : 0u);
+            }
           }
           issued = true;
           umma_commit_pair_multicast(&empty[s], 0x3);

@@ -217,9 +217,9 @@ cudaError_t launch_swapab_t(const LaunchArgs& a, DeviceSlot* slot, int config_bi
   return cudaGetLastError();
 }
 
-template <typename T, int STAGES, bool KM, int AP = 1>
+template <typename T, int STAGES, bool KM, int AP = 1, int KSUB = 1>
 cudaError_t launch_umma2_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit) {
-  using L = umma2::Smem<STAGES>;
+  using L = umma2::Smem<STAGES, KSUB>;
   TmaMapSet<AP> ta;
   CUtensorMap tb, td;
   const bool bf16 = a.bf16;
@@ -236,7 +236,7 @@ cudaError_t launch_umma2_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit
   p.k = static_cast<int>(a.k);
   p.tiles_m = static_cast<int>((a.m + umma2::kBlockM - 1) / umma2::kBlockM);
   p.tiles_n = static_cast<int>((a.n + umma2::kBlockN - 1) / umma2::kBlockN);
-  p.num_kb = static_cast<int>((a.k + umma2::kBlockK - 1) / umma2::kBlockK);
+  p.num_kb = static_cast<int>((a.k + KSUB * umma2::kBlockK - 1) / (KSUB * umma2::kBlockK));
   p.total_tiles = p.tiles_m * p.tiles_n;
   p.group_m = std::min(p.tiles_m, 8);
   p.alpha = a.alpha;
@@ -251,7 +251,7 @@ cudaError_t launch_umma2_t(const LaunchArgs& a, DeviceSlot* slot, int config_bit
   p.a_rows_per_part = AP == 1 ? 0 : static_cast<int>(a.a_rows_per_part);
   p.a_parts = AP == 1 ? 1 : a.a_nparts;
 
-  auto kernel = umma2::gemm_kernel<T, STAGES, KM, AP>;
+  auto kernel = umma2::gemm_kernel<T, STAGES, KM, AP, KSUB>;
   cudaError_t e = ensure_smem_attr(slot, config_bit, kernel, L::kDynamicBytes);
   if (e != cudaSuccess) return e;
 
@@ -731,11 +731,11 @@ cudaError_t launch_umma_pair_gemm(const LaunchArgs& a) {
   }
   const int off = a.b_col_major ? kCfgColMajorB : 0;
   if (a.b_col_major) {
-    return a.bf16 ? launch_umma2_t<__nv_bfloat16, 6, true>(a, slot, kCfgPairBf16 + off)
-                  : launch_umma2_t<half, 6, true>(a, slot, kCfgPairF16 + off);
+    return a.bf16 ? launch_umma2_t<__nv_bfloat16, 3, true, 1, 2>(a, slot, kCfgPairBf16 + off)
+                  : launch_umma2_t<half, 3, true, 1, 2>(a, slot, kCfgPairF16 + off);
   }
-  return a.bf16 ? launch_umma2_t<__nv_bfloat16, 6, false>(a, slot, kCfgPairBf16 + off)
-                : launch_umma2_t<half, 6, false>(a, slot, kCfgPairF16 + off);
+  return a.bf16 ? launch_umma2_t<__nv_bfloat16, 3, false, 1, 2>(a, slot, kCfgPairBf16 + off)
+                : launch_umma2_t<half, 3, false, 1, 2>(a, slot, kCfgPairF16 + off);
 }
 
 cudaError_t launch_umma_swapab_sk_gemm(const LaunchArgs& a) {
