@@ -47,9 +47,9 @@ MEASURED_PEAKS = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
 # the dominant kernel at TP1 -- gate_up 8192 x 28672 x 4096 on the 2-CTA
-# 256x256 kernel -- from one ncu capture of that exact launch (1183.8 MB read +
-# 457.6 MB written; algorithmic 301.9 MB read + 469.8 MB written).
-GATE_UP_TRAFFIC_BYTES = 1183789568 + 457606400
+# 256x256 kernel -- from one ncu capture of that exact launch (1113.3 MB read +
+# 455.4 MB written; algorithmic 301.9 MB read + 469.8 MB written).
+GATE_UP_TRAFFIC_BYTES = 1113329152 + 455350528
 
 NVML_REASONS = {
     0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
