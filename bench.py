@@ -9,8 +9,11 @@ o_proj [4096 x 4096] and down [4096 x 14336] row-parallel (K split, then an
 all-reduce of the BF16 partials: the library's NVLS kernel, or NCCL with
 --comm nccl). At TP > 1 the 8192 tokens run as two independent 4096-row
 blocks on two streams (--micro), so one block's all-reduce overlaps the other
-block's GEMMs. 3573 GFLOP per step for the whole job, whatever the rank
-count (strong scaling). --sp 1 runs the sequence-parallel form of the same
+block's GEMMs. The steps are replayed from CUDA graphs of up to 10 consecutive
+layer steps (--layers-per-graph) with the blocks joined only at each graph's
+ends, as a stack of layers runs: one block's next layer overlaps the other
+block's last all-reduce; every step does the whole layer's work. 3573 GFLOP
+per step for the whole job, whatever the rank count (strong scaling). --sp 1 runs the sequence-parallel form of the same
 step instead (reduce-scatters; qkv / gate_up get the other ranks' rows by
 copy-engine copies into local memory, or inside the GEMM with --sp-gather
 fused; NVLS only).
@@ -729,7 +732,7 @@ def main(argv=None) -> int:
                     help="independent row blocks per step, each on its own stream (0: 2 when TP > 1, else 1)")
     ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",
                     help="replay each step from a CUDA graph (auto: when TP > 1)")
-    ap.add_argument("--layers-per-graph", type=int, default=1,
+    ap.add_argument("--layers-per-graph", type=int, default=10,
                     help="at TP > 1 with row blocks: consecutive layer steps captured in one CUDA graph, the "
                          "blocks joined only at its ends (as a stack of layers runs), so one block's next layer "
                          "overlaps another block's last all-reduce; every step does the full layer's work")
