@@ -417,8 +417,8 @@ def run_gpu(args) -> int:
             # plus a one-step graph for the remainder of --steps
             graphs, per = capture_steps(lambda: layer.forward_overlapped_layers(x, streams, lpg), 1)
             launches_per_step = per // lpg
-            tail, _ = capture_steps(lambda: step(x), 1)
-            graphs += tail
+            # no name may keep a graph alive past graphs.clear(): they can hold NCCL calls
+            graphs += capture_steps(lambda: step(x), 1)[0]
         else:
             graphs, launches_per_step = capture_steps(lambda: step(x), 2 if sp else 1)
         for i in range(4):
